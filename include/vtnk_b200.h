@@ -1,0 +1,189 @@
+/*
+ * vtnk_b200 -- C ABI of the B200 (sm_100a) trie-constrained decoding step.
+ *
+ * Every entry point takes plain device pointers and sizes, launches on the
+ * given CUDA stream (NULL = legacy default stream), never synchronises the
+ * host, never allocates device memory and returns VTNK_OK or an error code
+ * (message via vtnk_last_error()).  Outputs are written in full, including
+ * the -1 / -inf padding the reference's ops pre-fill.
+ *
+ * Reference: EdoardoBotta/RecTokens, Python/Triton.  Each declaration cites the
+ * reference interface it replaces.
+ */
+#ifndef VTNK_B200_H
+#define VTNK_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types of the dense operands */
+enum { VTNK_F32 = 0, VTNK_BF16 = 1, VTNK_F16 = 2 };
+
+/* status codes */
+enum {
+  VTNK_OK = 0,
+  VTNK_ERR_ARG = 1,         /* bad argument (shape, stride, null pointer) */
+  VTNK_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  VTNK_ERR_UNSUPPORTED = 3, /* valid input this build does not handle */
+  VTNK_ERR_DEVICE = 4       /* a kernel reported a failure (bounded wait ran out) */
+};
+
+/* CSR trie: the reference's CompactCSRTrie (rectokens/schemas/compact_csr_trie.py:14-35).
+ * row_ptrs [n_nodes] int64 (no trailing nnz entry), cols = stacked_cols_vals[0],
+ * vals = stacked_cols_vals[1], both [nnz + 1] int64 with a -1 sentinel last. */
+typedef struct {
+  const int64_t* row_ptrs;
+  const int64_t* cols;
+  const int64_t* vals;
+  int64_t n_nodes;
+  int64_t nnz;
+} vtnk_csr_t;
+
+/* The fused linear operand: a [rows, hidden] (row stride a_stride elements,
+ * unit column stride), b = W.T viewed as [hidden, n_vocab] with element strides
+ * (b_stride_k, b_stride_n) -- the reference's (b_stride_K, b_stride_N),
+ * rectokens/kernels/constrained_node_transition.py:426-430.  bias [n_vocab] or
+ * NULL.  a, b and bias share `dtype`. */
+typedef struct {
+  const void* a;
+  int64_t rows;
+  int64_t hidden;
+  int64_t a_stride;
+  const void* b;
+  int64_t n_vocab;
+  int64_t b_stride_k;
+  int64_t b_stride_n;
+  const void* bias;
+  int32_t dtype;
+} vtnk_linear_t;
+
+/* Replaces vtnk::_constrained_node_transition_op
+ * (rectokens/kernels/constrained_node_transition.py:14-61): copy `logits`
+ * [B, N] (row stride logits_stride) to corrected_logits [B, N] (contiguous,
+ * same dtype) with every column that is not a child of cur_node[b] set to
+ * -inf; next_node / valid_idxs [B, max_branches] get the child node ids /
+ * tokens, -1 padded. */
+int vtnk_constrained_node_transition(const void* logits, int32_t dtype, int64_t B, int64_t N,
+                                     int64_t logits_stride, const int64_t* cur_node,
+                                     const vtnk_csr_t* csr, int64_t max_branches,
+                                     void* corrected_logits, int64_t* next_node,
+                                     int64_t* valid_idxs, void* stream);
+
+/* Replaces vtnk::_fused_linear_constrained_node_transition_op (kernels:388-447):
+ * corrected_logits [rows, n_vocab] fp32 = a @ b (+ bias) on child columns,
+ * -inf elsewhere; next_node / valid_idxs [rows, max_branches]. */
+int vtnk_fused_linear_constrained_node_transition(const vtnk_linear_t* lin,
+                                                  const int64_t* cur_node,
+                                                  const vtnk_csr_t* csr, int64_t max_branches,
+                                                  float* corrected_logits, int64_t* next_node,
+                                                  int64_t* valid_idxs, void* stream);
+
+/* Replaces vtnk::_fused_linear_constrained_node_transition_topk_op (kernels:791-853):
+ * topk_logits [rows, k] fp32 descending and topk_idxs [rows, k] token ids
+ * (-1 / -inf when a row has fewer than k children; ties go to the lower
+ * branch slot); next_node / valid_idxs [rows, max_branches].
+ * Requires 1 <= k <= max_branches (torch.topk raises otherwise). */
+int vtnk_fused_linear_constrained_node_transition_topk(const vtnk_linear_t* lin,
+                                                       const int64_t* cur_node,
+                                                       const vtnk_csr_t* csr, int64_t max_branches,
+                                                       int64_t k, int64_t* next_node,
+                                                       int64_t* valid_idxs, float* topk_logits,
+                                                       int64_t* topk_idxs, void* stream);
+
+/* Replaces vtnk::_fused_linear_constrained_node_transition_sampling_op
+ * (kernels:562-635): Gumbel-max sample per row, argmax over children of
+ * logit / T + g with g from Philox(seed, row * max_branches + slot) exactly as
+ * the reference's kernel draws it (kernels:359-380); sample [rows] fp32 token
+ * id, -1.0 when none.  temperature: device pointer to one fp32 (NULL = 1). */
+int vtnk_fused_linear_constrained_node_transition_sampling(
+    const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+    int64_t max_branches, uint64_t seed, const float* temperature, int64_t* next_node,
+    int64_t* valid_idxs, float* sample, void* stream);
+
+/* The Gumbel noise the sampling kernel adds at (row, slot), written to
+ * out [rows, max_branches] fp32 so a checker can replay a sampling call
+ * (kernels:372-374 formula; no reference counterpart as an entry point). */
+int vtnk_gumbel_noise(uint64_t seed, int64_t rows, int64_t max_branches, float* out,
+                      void* stream);
+
+/* One beam-search level, fused: for every row, the n_cand best children by
+ * logit (ties to the lower slot), their logits, tokens and child node ids, and
+ * the row's log-sum-exp over all children.  Replaces the per-level work of
+ * decode_one_step (rectokens/decoding/constrained_decoding.py:245-297: LM-head
+ * logits, constrained_node_transition, topk(beam_size), log_softmax) for the
+ * item-token rows of the head.  cur_node NULL = every row at the root.
+ * window_lo / window_n: a column range [window_lo, window_lo + window_n) that
+ * contains every child token of every row (window_n <= 256 enables the
+ * tcgen05 tile path for bf16); window_n = 0 when unknown.
+ * Outputs: cand_tok / cand_node int64 [rows, n_cand], cand_logit fp32
+ * [rows, n_cand] (-1 / -inf padded), row_lse fp32 [rows]. */
+int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+                   int64_t max_branches, int64_t n_cand, int64_t window_lo, int64_t window_n,
+                   int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
+                   void* stream);
+
+/* Beam merge (rectokens/decoding/constrained_decoding.py:305-349, next node
+ * :368-383).  level 0: each of the B queries keeps its k best of n_cand
+ * candidates (rows = B).  level > 0: total = prev_logp[parent] + cand logp over
+ * the k * n_cand candidates of a query (rows = B * k), the k best kept, ties to
+ * the lower candidate index.  prev_ids [B*k, level] int64; out_ids
+ * [B*k, level+1]; out_logp, out_node, out_parent [B*k]. */
+int vtnk_beam_merge(int64_t level, int64_t B, int64_t k, int64_t n_cand,
+                    const int64_t* cand_tok, const float* cand_logit, const int64_t* cand_node,
+                    const float* row_lse, const float* prev_logp, const int64_t* prev_ids,
+                    int64_t* out_ids, float* out_logp, int64_t* out_node, int64_t* out_parent,
+                    void* stream);
+
+/* A full L-level constrained beam search (autoregressive_generate with
+ * GenerationConfig(steps=L, k=beams, beam_size=n_cand, temperature=0),
+ * rectokens/decoding/constrained_decoding.py:140-179) for an LM whose item-token
+ * hidden state at level l is hidden[l] (rows = batch at level 0, batch * beams
+ * after, row stride hidden_stride).  weight = W [n_vocab, hidden] row-major. */
+typedef struct {
+  const void* const* hidden;          /* host array [levels] of device pointers */
+  int64_t hidden_stride;
+  const void* weight;
+  int64_t n_vocab;
+  int64_t hidden_dim;
+  const void* bias;
+  int32_t dtype;
+  vtnk_csr_t csr;
+  const int64_t* layer_max_branches;  /* host array [levels] */
+  const int64_t* window_lo;           /* host array [levels] or NULL */
+  const int64_t* window_n;            /* host array [levels] or NULL */
+  int64_t levels;
+  int64_t batch;
+  int64_t beams;
+  int64_t n_cand;
+} vtnk_search_t;
+
+/* Bytes of device scratch vtnk_beam_search needs for `s`. */
+size_t vtnk_beam_search_workspace_bytes(const vtnk_search_t* s);
+
+/* Runs the search; out_ids [batch*beams, levels] int64, out_logp
+ * [batch*beams] fp32, out_node [batch*beams] int64 (final trie node). */
+int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_bytes,
+                     int64_t* out_ids, float* out_logp, int64_t* out_node, void* stream);
+
+/* Synthetic hidden states (benchmark / test input generator, no reference
+ * counterpart): out[r, h] = table[mix64(key(seed, stream_id) ^ ((row0 + r) * H + h)) >> 48]
+ * with the 65,536-entry quantile table given as bf16 bits (dtype BF16) or fp32
+ * (dtype F32).  Same function as rectokens_b200/synthetic.py. */
+int vtnk_synth_normal(uint64_t seed, uint64_t stream_id, int64_t row0, int64_t rows,
+                      int64_t H, const void* table, int32_t dtype, void* out, void* stream);
+
+/* Human-readable description of the last error on this host thread. */
+const char* vtnk_last_error(void);
+
+/* Library ABI version (major * 100 + minor). */
+int vtnk_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VTNK_B200_H */

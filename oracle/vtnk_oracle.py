@@ -85,16 +85,19 @@ def branch_logits(a, b, bias, valid_idxs, acc=np.float64):
     Restates the contraction of kernels:273-356 / vntk.py:36-39 with the
     inputs' exact values accumulated in ``acc`` precision.
     """
-    a = np.asarray(a, dtype=acc)
-    bt = np.asarray(b, dtype=acc).T  # (N, H)
+    a = np.asarray(a)
+    bt = np.asarray(b).T  # (N, H), weight rows
     B, mb = valid_idxs.shape
     out = np.full((B, mb), -np.inf, dtype=np.float64)
-    r, s = np.nonzero(valid_idxs >= 0)
-    cols = valid_idxs[r, s]
-    vals = np.einsum("ij,ij->i", a[r], bt[cols])
-    if bias is not None:
-        vals = vals + np.asarray(bias, dtype=acc)[cols]
-    out[r, s] = vals
+    chunk = max(1, (1 << 25) // max(1, mb * a.shape[1]))  # bound the gathered block
+    for r0 in range(0, B, chunk):
+        vi = valid_idxs[r0:r0 + chunk]
+        wg = bt[np.maximum(vi, 0)].astype(acc, copy=False)          # (r, mb, H)
+        ar = a[r0:r0 + chunk].astype(acc, copy=False)[:, :, None]   # (r, H, 1)
+        vals = np.matmul(wg, ar)[:, :, 0]
+        if bias is not None:
+            vals = vals + np.asarray(bias, dtype=acc)[np.maximum(vi, 0)]
+        out[r0:r0 + chunk] = np.where(vi >= 0, vals, -np.inf)
     return out.astype(np.float32)
 
 

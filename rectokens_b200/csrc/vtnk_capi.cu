@@ -1,0 +1,359 @@
+// extern "C" entry points of libvtnk_b200: argument checks, dispatch, and the
+// device-resident beam-search driver.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "vtnk_common.cuh"
+#include "vtnk_internal.h"
+
+namespace vtnk {
+
+namespace {
+thread_local char g_err[512] = "";
+}
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return VTNK_OK;
+  set_error("%s: %s", what, cudaGetErrorString(e));
+  return VTNK_ERR_CUDA;
+}
+
+namespace {
+
+int elem_size(int dtype) { return dtype == VTNK_F32 ? 4 : 2; }
+
+int check_csr(const vtnk_csr_t* c) {
+  VTNK_REQUIRE(c != nullptr, "csr is NULL");
+  VTNK_REQUIRE(c->n_nodes >= 1 && c->nnz >= 0, "csr sizes invalid");
+  VTNK_REQUIRE(c->row_ptrs && c->cols && c->vals, "csr pointer is NULL");
+  return VTNK_OK;
+}
+
+int check_linear(const vtnk_linear_t* l) {
+  VTNK_REQUIRE(l != nullptr, "linear operand is NULL");
+  VTNK_REQUIRE(l->dtype == VTNK_F32 || l->dtype == VTNK_BF16 || l->dtype == VTNK_F16,
+               "unsupported dtype %d", l->dtype);
+  VTNK_REQUIRE(l->rows >= 0 && l->hidden >= 1 && l->n_vocab >= 1, "bad linear shape");
+  VTNK_REQUIRE(l->rows == 0 || (l->a && l->b), "linear pointer is NULL");
+  VTNK_REQUIRE(l->a_stride >= l->hidden, "a row stride < hidden");
+  return VTNK_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+RowsArgs rows_from(const vtnk_linear_t* l, const int64_t* cur_node, const vtnk_csr_t* c,
+                   int64_t mb) {
+  RowsArgs p{};
+  p.a = l->a;
+  p.rows = l->rows;
+  p.H = l->hidden;
+  p.a_stride = l->a_stride;
+  p.b = l->b;
+  p.N = l->n_vocab;
+  p.b_sk = l->b_stride_k;
+  p.b_sn = l->b_stride_n;
+  p.bias = l->bias;
+  p.cur_node = cur_node;
+  p.csr = make_csr(*c);
+  p.mb = mb;
+  const int v = 16 / elem_size(l->dtype);
+  p.vec = l->b_stride_k == 1 && (l->hidden % v) == 0 && (l->a_stride % v) == 0 &&
+          (l->b_stride_n % v) == 0 && aligned16(l->a) && aligned16(l->b);
+  return p;
+}
+
+int check_step(const vtnk_linear_t* l, const vtnk_csr_t* c, int64_t mb) {
+  int rc = check_linear(l);
+  if (rc) return rc;
+  rc = check_csr(c);
+  if (rc) return rc;
+  VTNK_REQUIRE(mb >= 0 && mb <= (1 << 20), "max_branches out of range");
+  return VTNK_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+struct SearchLayout {
+  size_t cand_tok, cand_node, cand_logit, lse, ids[2], logp[2], node[2], parent, total;
+};
+
+SearchLayout search_layout(const vtnk_search_t* s) {
+  const size_t bk = static_cast<size_t>(s->batch) * s->beams;
+  const size_t rmax = bk > static_cast<size_t>(s->batch) ? bk : s->batch;
+  const size_t nc = rmax * s->n_cand;
+  SearchLayout L{};
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += align256(bytes);
+    return o;
+  };
+  L.cand_tok = take(nc * 8);
+  L.cand_node = take(nc * 8);
+  L.cand_logit = take(nc * 4);
+  L.lse = take(rmax * 4);
+  for (int i = 0; i < 2; ++i) {
+    L.ids[i] = take(bk * s->levels * 8);
+    L.logp[i] = take(bk * 4);
+    L.node[i] = take(bk * 8);
+  }
+  L.parent = take(bk * 8);
+  L.total = off;
+  return L;
+}
+
+// One fused level: tcgen05 tile kernel when the shape allows, else rows kernel.
+int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+                   int64_t mb, int64_t n_cand, int64_t window_lo, int64_t window_n,
+                   int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
+                   cudaStream_t s) {
+  if (lin->rows == 0) return VTNK_OK;
+  if (tc_enabled() && lin->dtype == VTNK_BF16 && window_n > 0 && window_n <= 256 &&
+      lin->b_stride_k == 1 && lin->rows >= 128) {
+    TcArgs t{};
+    t.a = lin->a;
+    t.rows = lin->rows;
+    t.H = lin->hidden;
+    t.a_stride = lin->a_stride;
+    t.w = lin->b;
+    t.w_stride = lin->b_stride_n;
+    t.window_lo = window_lo;
+    t.window_n = static_cast<int>(window_n);
+    t.bias = lin->bias;
+    t.cur_node = cur_node;
+    t.csr = make_csr(*csr);
+    t.mb = mb;
+    t.n_cand = static_cast<int>(n_cand);
+    t.cand_tok = cand_tok;
+    t.cand_logit = cand_logit;
+    t.cand_node = cand_node;
+    t.row_lse = row_lse;
+    const int rc = launch_beam_step_tc(t, s);
+    if (rc != VTNK_ERR_UNSUPPORTED) return rc;
+  }
+  RowsArgs p = rows_from(lin, cur_node, csr, mb);
+  p.k = static_cast<int>(n_cand);
+  p.buf_cap = static_cast<int>(mb > 0 ? mb : 1);
+  p.out_logit = cand_logit;
+  p.out_tok = cand_tok;
+  p.out_node = cand_node;
+  p.out_lse = row_lse;
+  return launch_rows(p, MODE_BEAM, lin->dtype, s);
+}
+
+}  // namespace
+}  // namespace vtnk
+
+using namespace vtnk;
+
+extern "C" {
+
+const char* vtnk_last_error(void) { return g_err; }
+
+int vtnk_version(void) { return 100; }
+
+int vtnk_constrained_node_transition(const void* logits, int32_t dtype, int64_t B, int64_t N,
+                                     int64_t logits_stride, const int64_t* cur_node,
+                                     const vtnk_csr_t* csr, int64_t max_branches,
+                                     void* corrected_logits, int64_t* next_node,
+                                     int64_t* valid_idxs, void* stream) {
+  int rc = check_csr(csr);
+  if (rc) return rc;
+  VTNK_REQUIRE(B >= 0 && N >= 1 && logits_stride >= N, "bad logits shape");
+  VTNK_REQUIRE(max_branches >= 0, "max_branches < 0");
+  VTNK_REQUIRE(B == 0 || (logits && cur_node && corrected_logits), "NULL pointer");
+  VTNK_REQUIRE(B == 0 || max_branches == 0 || (next_node && valid_idxs), "NULL pointer");
+  return launch_mask(logits, dtype, B, N, logits_stride, cur_node, make_csr(*csr), max_branches,
+                     corrected_logits, next_node, valid_idxs, as_stream(stream));
+}
+
+int vtnk_fused_linear_constrained_node_transition(const vtnk_linear_t* lin,
+                                                  const int64_t* cur_node,
+                                                  const vtnk_csr_t* csr, int64_t max_branches,
+                                                  float* corrected_logits, int64_t* next_node,
+                                                  int64_t* valid_idxs, void* stream) {
+  int rc = check_step(lin, csr, max_branches);
+  if (rc) return rc;
+  VTNK_REQUIRE(lin->rows == 0 || (cur_node && corrected_logits), "NULL pointer");
+  VTNK_REQUIRE(lin->rows == 0 || max_branches == 0 || (next_node && valid_idxs), "NULL pointer");
+  RowsArgs p = rows_from(lin, cur_node, csr, max_branches);
+  p.corrected = corrected_logits;
+  p.next_node = next_node;
+  p.valid_idxs = valid_idxs;
+  return launch_rows(p, MODE_FUSED, lin->dtype, as_stream(stream));
+}
+
+int vtnk_fused_linear_constrained_node_transition_topk(const vtnk_linear_t* lin,
+                                                       const int64_t* cur_node,
+                                                       const vtnk_csr_t* csr, int64_t max_branches,
+                                                       int64_t k, int64_t* next_node,
+                                                       int64_t* valid_idxs, float* topk_logits,
+                                                       int64_t* topk_idxs, void* stream) {
+  int rc = check_step(lin, csr, max_branches);
+  if (rc) return rc;
+  VTNK_REQUIRE(k >= 1 && k <= max_branches, "k (%lld) must be in [1, max_branches=%lld]",
+               (long long)k, (long long)max_branches);
+  VTNK_REQUIRE(lin->rows == 0 || (cur_node && next_node && valid_idxs && topk_logits && topk_idxs),
+               "NULL pointer");
+  RowsArgs p = rows_from(lin, cur_node, csr, max_branches);
+  p.k = static_cast<int>(k);
+  p.buf_cap = static_cast<int>(max_branches);
+  p.next_node = next_node;
+  p.valid_idxs = valid_idxs;
+  p.out_logit = topk_logits;
+  p.out_tok = topk_idxs;
+  return launch_rows(p, MODE_TOPK, lin->dtype, as_stream(stream));
+}
+
+int vtnk_fused_linear_constrained_node_transition_sampling(
+    const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+    int64_t max_branches, uint64_t seed, const float* temperature, int64_t* next_node,
+    int64_t* valid_idxs, float* sample, void* stream) {
+  int rc = check_step(lin, csr, max_branches);
+  if (rc) return rc;
+  VTNK_REQUIRE(lin->rows == 0 || (cur_node && sample), "NULL pointer");
+  VTNK_REQUIRE(lin->rows == 0 || max_branches == 0 || (next_node && valid_idxs), "NULL pointer");
+  RowsArgs p = rows_from(lin, cur_node, csr, max_branches);
+  p.seed = seed;
+  p.temperature = temperature;
+  p.buf_cap = static_cast<int>(max_branches > 0 ? max_branches : 1);
+  p.next_node = next_node;
+  p.valid_idxs = valid_idxs;
+  p.sample = sample;
+  return launch_rows(p, MODE_SAMPLE, lin->dtype, as_stream(stream));
+}
+
+int vtnk_gumbel_noise(uint64_t seed, int64_t rows, int64_t max_branches, float* out,
+                      void* stream) {
+  VTNK_REQUIRE(rows >= 0 && max_branches >= 0, "bad shape");
+  VTNK_REQUIRE(rows * max_branches == 0 || out, "NULL pointer");
+  return launch_gumbel(seed, rows, max_branches, out, as_stream(stream));
+}
+
+int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+                   int64_t max_branches, int64_t n_cand, int64_t window_lo, int64_t window_n,
+                   int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
+                   void* stream) {
+  int rc = check_step(lin, csr, max_branches);
+  if (rc) return rc;
+  VTNK_REQUIRE(n_cand >= 1 && n_cand <= 1024, "n_cand out of range");
+  VTNK_REQUIRE(window_n >= 0, "window_n < 0");
+  VTNK_REQUIRE(lin->rows == 0 || (cand_tok && cand_logit && cand_node && row_lse),
+               "NULL pointer");
+  return beam_step_impl(lin, cur_node, csr, max_branches, n_cand, window_lo, window_n, cand_tok,
+                        cand_logit, cand_node, row_lse, as_stream(stream));
+}
+
+int vtnk_beam_merge(int64_t level, int64_t B, int64_t k, int64_t n_cand,
+                    const int64_t* cand_tok, const float* cand_logit, const int64_t* cand_node,
+                    const float* row_lse, const float* prev_logp, const int64_t* prev_ids,
+                    int64_t* out_ids, float* out_logp, int64_t* out_node, int64_t* out_parent,
+                    void* stream) {
+  VTNK_REQUIRE(level >= 0 && B >= 0 && k >= 1 && n_cand >= 1, "bad merge sizes");
+  VTNK_REQUIRE(level > 0 || k <= n_cand, "first level needs k <= n_cand");
+  VTNK_REQUIRE(B == 0 || (cand_tok && cand_logit && cand_node && row_lse && out_ids && out_logp &&
+                          out_node && out_parent),
+               "NULL pointer");
+  VTNK_REQUIRE(level == 0 || B == 0 || (prev_logp && prev_ids), "NULL previous beams");
+  MergeArgs p{};
+  p.level = level;
+  p.B = B;
+  p.k = static_cast<int>(k);
+  p.n_cand = static_cast<int>(n_cand);
+  p.cap = static_cast<int>(level == 0 ? n_cand : k * n_cand);
+  p.cand_tok = cand_tok;
+  p.cand_logit = cand_logit;
+  p.cand_node = cand_node;
+  p.row_lse = row_lse;
+  p.prev_logp = prev_logp;
+  p.prev_ids = prev_ids;
+  p.out_ids = out_ids;
+  p.out_logp = out_logp;
+  p.out_node = out_node;
+  p.out_parent = out_parent;
+  return launch_merge(p, as_stream(stream));
+}
+
+size_t vtnk_beam_search_workspace_bytes(const vtnk_search_t* s) {
+  if (!s) return 0;
+  return search_layout(s).total;
+}
+
+int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_bytes,
+                     int64_t* out_ids, float* out_logp, int64_t* out_node, void* stream) {
+  VTNK_REQUIRE(s != nullptr, "search is NULL");
+  VTNK_REQUIRE(s->levels >= 1 && s->batch >= 0 && s->beams >= 1 && s->n_cand >= 1,
+               "bad search sizes");
+  VTNK_REQUIRE(s->beams <= s->n_cand, "beams must not exceed candidates per beam");
+  VTNK_REQUIRE(s->hidden && s->weight && s->layer_max_branches, "NULL search pointer");
+  int rc = check_csr(&s->csr);
+  if (rc) return rc;
+  if (s->batch == 0) return VTNK_OK;
+  const SearchLayout L = search_layout(s);
+  VTNK_REQUIRE(workspace && workspace_bytes >= L.total, "workspace too small (%zu < %zu)",
+               workspace_bytes, L.total);
+  VTNK_REQUIRE(out_ids && out_logp && out_node, "NULL output");
+  char* ws = static_cast<char*>(workspace);
+  auto at = [&](size_t off) { return static_cast<void*>(ws + off); };
+  int64_t* cand_tok = static_cast<int64_t*>(at(L.cand_tok));
+  int64_t* cand_node = static_cast<int64_t*>(at(L.cand_node));
+  float* cand_logit = static_cast<float*>(at(L.cand_logit));
+  float* lse = static_cast<float*>(at(L.lse));
+  int64_t* parent = static_cast<int64_t*>(at(L.parent));
+  cudaStream_t st = as_stream(stream);
+
+  const int64_t* prev_node = nullptr;
+  const float* prev_logp = nullptr;
+  const int64_t* prev_ids = nullptr;
+  for (int64_t level = 0; level < s->levels; ++level) {
+    vtnk_linear_t lin{};
+    lin.a = s->hidden[level];
+    lin.rows = level == 0 ? s->batch : s->batch * s->beams;
+    lin.hidden = s->hidden_dim;
+    lin.a_stride = s->hidden_stride;
+    lin.b = s->weight;
+    lin.n_vocab = s->n_vocab;
+    lin.b_stride_k = 1;
+    lin.b_stride_n = s->hidden_dim;
+    lin.bias = s->bias;
+    lin.dtype = s->dtype;
+    rc = check_linear(&lin);
+    if (rc) return rc;
+    const int64_t wlo = s->window_lo ? s->window_lo[level] : 0;
+    const int64_t wn = s->window_n ? s->window_n[level] : 0;
+    rc = beam_step_impl(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand, wlo, wn,
+                        cand_tok, cand_logit, cand_node, lse, st);
+    if (rc) return rc;
+    const bool last = level + 1 == s->levels;
+    const int slot = static_cast<int>(level & 1);
+    int64_t* ids = last ? out_ids : static_cast<int64_t*>(at(L.ids[slot]));
+    float* logp = last ? out_logp : static_cast<float*>(at(L.logp[slot]));
+    int64_t* node = last ? out_node : static_cast<int64_t*>(at(L.node[slot]));
+    rc = vtnk_beam_merge(level, s->batch, s->beams, s->n_cand, cand_tok, cand_logit, cand_node, lse,
+                         prev_logp, prev_ids, ids, logp, node, parent, stream);
+    if (rc) return rc;
+    prev_node = node;
+    prev_logp = logp;
+    prev_ids = ids;
+  }
+  return VTNK_OK;
+}
+
+int vtnk_synth_normal(uint64_t seed, uint64_t stream_id, int64_t row0, int64_t rows, int64_t H,
+                      const void* table, int32_t dtype, void* out, void* stream) {
+  VTNK_REQUIRE(rows >= 0 && H >= 1 && row0 >= 0, "bad synth shape");
+  VTNK_REQUIRE(rows == 0 || (table && out), "NULL pointer");
+  VTNK_REQUIRE(dtype == VTNK_F32 || dtype == VTNK_BF16, "synth dtype must be F32 or BF16");
+  const uint64_t key = mix64((seed << 20) ^ stream_id);
+  return launch_synth(key, row0 * H, rows * H, table, dtype, out, as_stream(stream));
+}
+
+}  // extern "C"

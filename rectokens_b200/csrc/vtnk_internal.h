@@ -1,0 +1,86 @@
+// Internal launch interfaces shared by the vtnk_b200 translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "vtnk_common.cuh"
+
+namespace vtnk {
+
+enum { MODE_FUSED = 0, MODE_TOPK = 1, MODE_SAMPLE = 2, MODE_BEAM = 3 };
+
+struct RowsArgs {
+  const void* a;
+  int64_t rows, H, a_stride;
+  const void* b;
+  int64_t N, b_sk, b_sn;
+  const void* bias;
+  const int64_t* cur_node;  // nullptr: every row at the root
+  Csr csr;
+  int64_t mb;
+  int k;                    // top-k (MODE_TOPK) or candidates per row (MODE_BEAM)
+  uint64_t seed;
+  const float* temperature;
+  bool vec;                 // 16-byte vector loads of a and W rows are legal
+  int buf_cap;              // shared-memory floats per warp
+  float* corrected;         // MODE_FUSED  [rows, N]
+  int64_t* next_node;       // MODE_FUSED/TOPK/SAMPLE [rows, mb]
+  int64_t* valid_idxs;
+  float* out_logit;         // MODE_TOPK topk_logits / MODE_BEAM cand_logit [rows, k]
+  int64_t* out_tok;         // MODE_TOPK topk_idxs / MODE_BEAM cand_tok
+  int64_t* out_node;        // MODE_BEAM cand_node
+  float* out_lse;           // MODE_BEAM [rows]
+  float* sample;            // MODE_SAMPLE [rows]
+};
+
+struct MergeArgs {
+  int64_t level, B;
+  int k, n_cand, cap;
+  const int64_t* cand_tok;
+  const float* cand_logit;
+  const int64_t* cand_node;
+  const float* row_lse;
+  const float* prev_logp;
+  const int64_t* prev_ids;
+  int64_t* out_ids;
+  float* out_logp;
+  int64_t* out_node;
+  int64_t* out_parent;
+};
+
+// Tensor-core beam step (vtnk_tc.cu).
+struct TcArgs {
+  const void* a;            // bf16 [rows, H], row stride a_stride
+  int64_t rows, H, a_stride;
+  const void* w;            // bf16 W rows [N, H] (row stride w_stride), window rows used
+  int64_t w_stride;
+  int64_t window_lo;        // first token of the column window
+  int window_n;             // <= 256
+  const void* bias;         // bf16 [N] or nullptr
+  const int64_t* cur_node;  // nullptr: root
+  Csr csr;
+  int64_t mb;
+  int n_cand;
+  int64_t* cand_tok;
+  float* cand_logit;
+  int64_t* cand_node;
+  float* row_lse;
+  int* status;              // device word: 0 ok, else a failure code
+};
+
+int launch_rows(const RowsArgs& p, int mode, int dtype, cudaStream_t s);
+int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
+                const int64_t* cur_node, const Csr& csr, int64_t mb, void* out, int64_t* nn,
+                int64_t* vi, cudaStream_t s);
+int launch_merge(const MergeArgs& p, cudaStream_t s);
+int launch_synth(uint64_t key, int64_t e0, int64_t count, const void* table, int dtype, void* out,
+                 cudaStream_t s);
+int launch_gumbel(uint64_t seed, int64_t rows, int64_t mb, float* out, cudaStream_t s);
+
+// Returns VTNK_ERR_UNSUPPORTED (without launching) when the shape does not
+// fit the tile kernel; the caller then uses the row kernel.
+int launch_beam_step_tc(const TcArgs& p, cudaStream_t s);
+bool tc_enabled();
+
+}  // namespace vtnk

@@ -1,0 +1,393 @@
+// Warp-per-row kernels of the constrained decoding step (CUDA cores).
+//
+// One warp owns one row (beam) end to end: it reads the row's CSR slice,
+// computes the logit of every child (a[row] . W[col]) with 16-byte vector
+// loads, and finishes the row in registers / shared memory -- dense masked
+// logits, top-k, Gumbel-max or beam candidates -- so no cross-warp or
+// cross-CTA reduction is needed (the reference's sampling kernel merges CTAs
+// under a global spin lock, rectokens/kernels/constrained_node_transition.py:761-783).
+//
+// This path serves every shape: rows < 128, windows wider than one tensor-core
+// tile, fp32 / fp16 operands and arbitrary b strides.  bf16 rows >= 128 with a
+// <= 256-column window go to the tcgen05 tile kernel (vtnk_tc.cu).
+#include <climits>
+
+#include "vtnk_common.cuh"
+#include "vtnk_internal.h"
+
+namespace vtnk {
+
+namespace {
+
+constexpr int kWarps = 8;   // rows per CTA
+constexpr int kGroup = 4;   // children whose dot products share one pass over a[row]
+
+template <typename T, int MODE, bool VEC>
+__global__ void __launch_bounds__(kWarps * 32)
+rows_kernel(const RowsArgs p) {
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  float* buf = smem + warp * p.buf_cap;
+  const T* A = static_cast<const T*>(p.a);
+  const T* Bm = static_cast<const T*>(p.b);
+  const T* bias = static_cast<const T*>(p.bias);
+  const int64_t* cols = p.csr.cols;
+  const int64_t* vals = p.csr.vals;
+
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp; row < p.rows;
+       row += static_cast<int64_t>(gridDim.x) * kWarps) {
+    const int64_t cur = p.cur_node ? __ldg(p.cur_node + row) : 0;
+    int64_t start;
+    int count;
+    node_children(p.csr, cur, p.mb, start, count);
+
+    if (MODE != MODE_BEAM) {  // branch tables [rows, mb], -1 padded
+      int64_t* vi = p.valid_idxs + row * p.mb;
+      int64_t* nn = p.next_node + row * p.mb;
+      for (int j = lane; j < p.mb; j += 32) {
+        const bool ok = j < count;
+        vi[j] = ok ? __ldg(cols + start + j) : -1;
+        nn[j] = ok ? __ldg(vals + start + j) : -1;
+      }
+    }
+    float* crow = nullptr;
+    if (MODE == MODE_FUSED) {
+      crow = p.corrected + row * p.N;
+      if ((p.N & 3) == 0) {
+        float4* c4 = reinterpret_cast<float4*>(crow);
+        const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        for (int64_t n = lane; n < p.N / 4; n += 32) c4[n] = ninf;
+      } else {
+        for (int64_t n = lane; n < p.N; n += 32) crow[n] = -INFINITY;
+      }
+      __syncwarp();  // orders the fill before lane 0's child stores below
+    }
+
+    const T* arow = A + row * p.a_stride;
+    for (int base = 0; base < count; base += kGroup) {
+      int64_t col[kGroup];
+#pragma unroll
+      for (int g = 0; g < kGroup; ++g) {
+        const int j = base + g;
+        int64_t c = (j < count) ? __ldg(cols + start + j) : -1;
+        col[g] = (c >= 0 && c < p.N) ? c : -1;
+      }
+      float acc[kGroup];
+#pragma unroll
+      for (int g = 0; g < kGroup; ++g) acc[g] = 0.f;
+      if (VEC) {
+        constexpr int V = Vec16<T>::N;
+        for (int64_t h = static_cast<int64_t>(lane) * V; h < p.H; h += 32 * V) {
+          Vec16<T> av;
+          av.load(arow + h);
+#pragma unroll
+          for (int g = 0; g < kGroup; ++g) {
+            if (col[g] < 0) continue;
+            Vec16<T> bv;
+            bv.load(Bm + col[g] * p.b_sn + h);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc[g] = fmaf(av.v[i], bv.v[i], acc[g]);
+          }
+        }
+      } else {
+        for (int64_t h = lane; h < p.H; h += 32) {
+          const float av = to_f32<T>(arow[h]);
+#pragma unroll
+          for (int g = 0; g < kGroup; ++g) {
+            if (col[g] < 0) continue;
+            acc[g] = fmaf(av, to_f32<T>(Bm[h * p.b_sk + col[g] * p.b_sn]), acc[g]);
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < kGroup; ++g) {
+        const int j = base + g;
+        const float s = warp_sum(acc[g]);
+        if (j >= count || lane != 0) continue;
+        float v = -INFINITY;
+        if (col[g] >= 0) {
+          v = s;
+          if (bias) v += to_f32<T>(bias[col[g]]);
+        }
+        if (MODE == MODE_FUSED) {
+          if (col[g] >= 0) crow[col[g]] = v;
+        } else {
+          buf[j] = v;
+        }
+      }
+    }
+    __syncwarp();
+
+    if (MODE == MODE_BEAM) {  // row log-sum-exp over every child
+      float m = -INFINITY;
+      for (int j = lane; j < count; j += 32) m = fmaxf(m, buf[j]);
+      m = warp_max(m);
+      float s = 0.f;
+      if (m > -INFINITY)
+        for (int j = lane; j < count; j += 32) s += expf(buf[j] - m);
+      s = warp_sum(s);
+      if (lane == 0) p.out_lse[row] = (m > -INFINITY) ? m + logf(s) : -INFINITY;
+    }
+
+    if (MODE == MODE_TOPK || MODE == MODE_BEAM) {
+      for (int r = 0; r < p.k; ++r) {
+        float bv = -INFINITY;
+        int bj = INT_MAX;
+        for (int j = lane; j < count; j += 32) {
+          const float v = buf[j];
+          if (v > bv || (v == bv && j < bj)) {
+            bv = v;
+            bj = j;
+          }
+        }
+        warp_argmax(bv, bj);
+        if (lane == 0) {
+          const int64_t o = row * p.k + r;
+          const bool ok = bj != INT_MAX && bv > -INFINITY;
+          p.out_logit[o] = ok ? bv : -INFINITY;
+          p.out_tok[o] = ok ? __ldg(cols + start + bj) : -1;
+          if (MODE == MODE_BEAM) p.out_node[o] = ok ? __ldg(vals + start + bj) : -1;
+          if (bj != INT_MAX) buf[bj] = __int_as_float(0x7fc00000);  // taken
+        }
+        __syncwarp();
+      }
+    }
+
+    if (MODE == MODE_SAMPLE) {
+      const float t = p.temperature ? __ldg(p.temperature) : 1.f;
+      float bv = -INFINITY;
+      int bj = INT_MAX;
+      for (int j = lane; j < count; j += 32) {
+        const float g = gumbel_at(p.seed, static_cast<uint32_t>(row * p.mb + j));
+        const float s = buf[j] / t + g;
+        if (s > bv) {  // slots visited in increasing order: first maximum kept
+          bv = s;
+          bj = j;
+        }
+      }
+      warp_argmax(bv, bj);
+      if (lane == 0)
+        p.sample[row] = (bj != INT_MAX && bv > -INFINITY)
+                            ? static_cast<float>(__ldg(cols + start + bj))
+                            : -1.f;
+    }
+    __syncwarp();
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32)
+mask_kernel(const T* __restrict__ logits, int64_t B, int64_t N, int64_t ls,
+            const int64_t* __restrict__ cur_node, const Csr csr, int64_t mb, T* __restrict__ out,
+            int64_t* __restrict__ next_node, int64_t* __restrict__ valid_idxs) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const T ninf = from_f32<T>(-INFINITY);
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp; row < B;
+       row += static_cast<int64_t>(gridDim.x) * kWarps) {
+    int64_t start;
+    int count;
+    node_children(csr, cur_node[row], mb, start, count);
+    for (int j = lane; j < mb; j += 32) {
+      const bool ok = j < count;
+      valid_idxs[row * mb + j] = ok ? __ldg(csr.cols + start + j) : -1;
+      next_node[row * mb + j] = ok ? __ldg(csr.vals + start + j) : -1;
+    }
+    T* orow = out + row * N;
+    for (int64_t n = lane; n < N; n += 32) orow[n] = ninf;
+    __syncwarp();
+    for (int j = lane; j < count; j += 32) {
+      const int64_t c = __ldg(csr.cols + start + j);
+      if (c >= 0 && c < N) orow[c] = logits[row * ls + c];
+    }
+    __syncwarp();
+  }
+}
+
+// Beam merge: one warp per query.
+constexpr int kMergeWarps = 4;
+
+__global__ void __launch_bounds__(kMergeWarps * 32)
+merge_kernel(const MergeArgs p) {
+  extern __shared__ float msm[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t b = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
+  if (b >= p.B) return;
+  const int ncand = p.level == 0 ? p.n_cand : p.k * p.n_cand;
+  float* tot = msm + warp * p.cap;
+  int64_t* chosen = reinterpret_cast<int64_t*>(msm + kMergeWarps * p.cap) + warp * p.k;
+
+  for (int c = lane; c < ncand; c += 32) {
+    const int64_t row = p.level == 0 ? b : b * p.k + c / p.n_cand;
+    const int64_t e = row * p.n_cand + c % p.n_cand;
+    const float lp = (p.cand_tok[e] >= 0) ? p.cand_logit[e] - p.row_lse[row] : -INFINITY;
+    tot[c] = p.level == 0 ? lp : p.prev_logp[row] + lp;
+  }
+  __syncwarp();
+  for (int r = 0; r < p.k; ++r) {
+    float bv = -INFINITY;
+    int bc = INT_MAX;
+    for (int c = lane; c < ncand; c += 32) {
+      const float v = tot[c];
+      if (v > bv || (v == bv && c < bc)) {
+        bv = v;
+        bc = c;
+      }
+    }
+    warp_argmax(bv, bc);
+    if (lane == 0) {
+      const int64_t o = b * p.k + r;
+      const int64_t parent = p.level == 0 ? b : b * p.k + bc / p.n_cand;
+      const int64_t e = parent * p.n_cand + bc % p.n_cand;
+      p.out_logp[o] = bv;
+      p.out_node[o] = p.cand_node[e];
+      p.out_parent[o] = p.level == 0 ? b : parent;
+      p.out_ids[o * (p.level + 1) + p.level] = p.cand_tok[e];
+      chosen[r] = parent;
+      tot[bc] = __int_as_float(0x7fc00000);
+    }
+    __syncwarp();
+  }
+  if (p.level > 0) {  // copy each new beam's history from its parent
+    const int w = static_cast<int>(p.level);
+    for (int t = lane; t < p.k * w; t += 32) {
+      const int r = t / w, i = t % w;
+      p.out_ids[(b * p.k + r) * (w + 1) + i] = p.prev_ids[chosen[r] * w + i];
+    }
+  }
+}
+
+template <typename T>
+__global__ void synth_kernel(uint64_t key, int64_t e0, int64_t count, const T* __restrict__ table,
+                             T* __restrict__ out) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < count;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t z = mix64(static_cast<uint64_t>(e0 + i) ^ key);
+    out[i] = table[z >> 48];
+  }
+}
+
+__global__ void gumbel_kernel(uint64_t seed, int64_t rows, int64_t mb, float* out) {
+  const int64_t n = rows * mb;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    out[i] = gumbel_at(seed, static_cast<uint32_t>(i));
+}
+
+int grid_for(int64_t items, int per_block) {
+  int64_t g = (items + per_block - 1) / per_block;
+  const int64_t cap = 148LL * 64;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return static_cast<int>(g);
+}
+
+template <typename T, int MODE>
+int launch_rows_t(const RowsArgs& p, cudaStream_t s) {
+  const size_t sm = static_cast<size_t>(kWarps) * p.buf_cap * sizeof(float);
+  const int grid = grid_for(p.rows, kWarps);
+  if (p.vec) {
+    auto k = rows_kernel<T, MODE, true>;
+    if (sm > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    k<<<grid, kWarps * 32, sm, s>>>(p);
+  } else {
+    auto k = rows_kernel<T, MODE, false>;
+    if (sm > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    k<<<grid, kWarps * 32, sm, s>>>(p);
+  }
+  return cuda_status(cudaGetLastError(), "rows_kernel launch");
+}
+
+template <int MODE>
+int launch_rows_mode(const RowsArgs& p, int dtype, cudaStream_t s) {
+  switch (dtype) {
+    case VTNK_F32: return launch_rows_t<float, MODE>(p, s);
+    case VTNK_BF16: return launch_rows_t<__nv_bfloat16, MODE>(p, s);
+    case VTNK_F16: return launch_rows_t<__half, MODE>(p, s);
+  }
+  set_error("unsupported dtype %d", dtype);
+  return VTNK_ERR_ARG;
+}
+
+}  // namespace
+
+int launch_rows(const RowsArgs& p, int mode, int dtype, cudaStream_t s) {
+  if (p.rows == 0) return VTNK_OK;
+  const size_t sm = static_cast<size_t>(kWarps) * p.buf_cap * sizeof(float);
+  if (sm > 200 * 1024) {
+    set_error("max_branches %lld too large for the row kernel", (long long)p.mb);
+    return VTNK_ERR_UNSUPPORTED;
+  }
+  switch (mode) {
+    case MODE_FUSED: return launch_rows_mode<MODE_FUSED>(p, dtype, s);
+    case MODE_TOPK: return launch_rows_mode<MODE_TOPK>(p, dtype, s);
+    case MODE_SAMPLE: return launch_rows_mode<MODE_SAMPLE>(p, dtype, s);
+    case MODE_BEAM: return launch_rows_mode<MODE_BEAM>(p, dtype, s);
+  }
+  set_error("bad mode");
+  return VTNK_ERR_ARG;
+}
+
+int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
+                const int64_t* cur_node, const Csr& csr, int64_t mb, void* out, int64_t* nn,
+                int64_t* vi, cudaStream_t s) {
+  if (B == 0) return VTNK_OK;
+  const int grid = grid_for(B, kWarps);
+  switch (dtype) {
+    case VTNK_F32:
+      mask_kernel<float><<<grid, kWarps * 32, 0, s>>>(static_cast<const float*>(logits), B, N, ls,
+                                                      cur_node, csr, mb, static_cast<float*>(out), nn, vi);
+      break;
+    case VTNK_BF16:
+      mask_kernel<__nv_bfloat16><<<grid, kWarps * 32, 0, s>>>(
+          static_cast<const __nv_bfloat16*>(logits), B, N, ls, cur_node, csr, mb,
+          static_cast<__nv_bfloat16*>(out), nn, vi);
+      break;
+    case VTNK_F16:
+      mask_kernel<__half><<<grid, kWarps * 32, 0, s>>>(static_cast<const __half*>(logits), B, N, ls,
+                                                       cur_node, csr, mb, static_cast<__half*>(out), nn, vi);
+      break;
+    default:
+      set_error("unsupported dtype %d", dtype);
+      return VTNK_ERR_ARG;
+  }
+  return cuda_status(cudaGetLastError(), "mask_kernel launch");
+}
+
+int launch_merge(const MergeArgs& p, cudaStream_t s) {
+  if (p.B == 0) return VTNK_OK;
+  const size_t sm = static_cast<size_t>(kMergeWarps) * p.cap * sizeof(float) +
+                    static_cast<size_t>(kMergeWarps) * p.k * sizeof(int64_t);
+  if (sm > 200 * 1024) {
+    set_error("beams * candidates too large for the merge kernel");
+    return VTNK_ERR_UNSUPPORTED;
+  }
+  if (sm > 48 * 1024)
+    cudaFuncSetAttribute(merge_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  const int grid = static_cast<int>((p.B + kMergeWarps - 1) / kMergeWarps);
+  merge_kernel<<<grid, kMergeWarps * 32, sm, s>>>(p);
+  return cuda_status(cudaGetLastError(), "merge_kernel launch");
+}
+
+int launch_synth(uint64_t key, int64_t e0, int64_t count, const void* table, int dtype, void* out,
+                 cudaStream_t s) {
+  if (count == 0) return VTNK_OK;
+  const int grid = grid_for(count, 256 * 8);
+  if (dtype == VTNK_BF16 || dtype == VTNK_F16)
+    synth_kernel<uint16_t><<<grid, 256, 0, s>>>(key, e0, count, static_cast<const uint16_t*>(table),
+                                                static_cast<uint16_t*>(out));
+  else
+    synth_kernel<float><<<grid, 256, 0, s>>>(key, e0, count, static_cast<const float*>(table),
+                                             static_cast<float*>(out));
+  return cuda_status(cudaGetLastError(), "synth_kernel launch");
+}
+
+int launch_gumbel(uint64_t seed, int64_t rows, int64_t mb, float* out, cudaStream_t s) {
+  if (rows * mb == 0) return VTNK_OK;
+  gumbel_kernel<<<grid_for(rows * mb, 256 * 4), 256, 0, s>>>(seed, rows, mb, out);
+  return cuda_status(cudaGetLastError(), "gumbel_kernel launch");
+}
+
+}  // namespace vtnk
