@@ -256,6 +256,7 @@ def main():
         beam_merge,
         beam_step,
         constrained_beam_search_from_host,
+        child_index,
         level_windows,
     )
     from rectokens_b200.schemas import GenerationConfig
@@ -264,6 +265,7 @@ def main():
     cfg = GenerationConfig(steps=w.levels, k=w.beams, beam_size=w.topk, temperature=0.0)
     dw = WL.make_device_workload(w, dev, shard=rank, n_shards=world)
     wins = level_windows(dw.trie)
+    idxs = [child_index(dw.trie, l) for l in range(w.levels)]
     Bq, k = dw.batch, w.beams
 
     # preallocated per-level buffers: the timed loop allocates nothing
@@ -298,7 +300,7 @@ def main():
                 events[level][0].record(stream)
             L.check(lib.vtnk_beam_step(lins[level], L.ptr(cur), csr,
                                        dw.trie.layer_max_branches[level], w.topk,
-                                       wins[level][0], wins[level][1], b["tok"].data_ptr(),
+                                       idxs[level], b["tok"].data_ptr(),
                                        b["logit"].data_ptr(), b["node"].data_ptr(),
                                        b["lse"].data_ptr(), sptr))
             if events is not None:

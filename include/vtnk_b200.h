@@ -110,19 +110,37 @@ int vtnk_fused_linear_constrained_node_transition_sampling(
 int vtnk_gumbel_noise(uint64_t seed, int64_t rows, int64_t max_branches, float* out,
                       void* stream);
 
+/* Child-bitmask index of one trie depth, for the tensor-core beam step: for
+ * every node id in [node_lo, node_hi) a 256-bit mask (8 uint32 words, bit i =
+ * token window_lo + i is a child).  A node whose children are not in
+ * ascending token order or not all inside the window has an all-zero mask
+ * (its rows are then computed by an exact per-row path).  Derived data: the
+ * CSR arrays stay the reference layout; no reference counterpart. */
+typedef struct {
+  const uint32_t* masks;  /* [node_hi - node_lo, 8], 16-byte aligned */
+  int64_t node_lo;
+  int64_t node_hi;
+  int64_t window_lo;
+  int64_t window_n;       /* 1..256 */
+} vtnk_child_index_t;
+
+/* Builds index->masks (caller memory, (node_hi - node_lo) * 32 bytes) for
+ * the nodes and window described by `index` (no reference counterpart). */
+int vtnk_build_child_index(const vtnk_csr_t* csr, const vtnk_child_index_t* index,
+                           void* stream);
+
 /* One beam-search level, fused: for every row, the n_cand best children by
  * logit (ties to the lower slot), their logits, tokens and child node ids, and
  * the row's log-sum-exp over all children.  Replaces the per-level work of
  * decode_one_step (rectokens/decoding/constrained_decoding.py:245-297: LM-head
  * logits, constrained_node_transition, topk(beam_size), log_softmax) for the
  * item-token rows of the head.  cur_node NULL = every row at the root.
- * window_lo / window_n: a column range [window_lo, window_lo + window_n) that
- * contains every child token of every row (window_n <= 256 enables the
- * tcgen05 tile path for bf16); window_n = 0 when unknown.
+ * index: the child-bitmask index of this depth (enables the tcgen05 tile
+ * kernel for bf16, rows >= 128, n_cand <= 32), or NULL (CUDA-core row kernel).
  * Outputs: cand_tok / cand_node int64 [rows, n_cand], cand_logit fp32
  * [rows, n_cand] (-1 / -inf padded), row_lse fp32 [rows]. */
 int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
-                   int64_t max_branches, int64_t n_cand, int64_t window_lo, int64_t window_n,
+                   int64_t max_branches, int64_t n_cand, const vtnk_child_index_t* index,
                    int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
                    void* stream);
 
@@ -153,8 +171,8 @@ typedef struct {
   int32_t dtype;
   vtnk_csr_t csr;
   const int64_t* layer_max_branches;  /* host array [levels] */
-  const int64_t* window_lo;           /* host array [levels] or NULL */
-  const int64_t* window_n;            /* host array [levels] or NULL */
+  const vtnk_child_index_t* index;    /* host array [levels] (entries with masks
+                                         NULL use the row kernel), or NULL */
   int64_t levels;
   int64_t batch;
   int64_t beams;
@@ -175,6 +193,13 @@ int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_b
  * (dtype F32).  Same function as rectokens_b200/synthetic.py. */
 int vtnk_synth_normal(uint64_t seed, uint64_t stream_id, int64_t row0, int64_t rows,
                       int64_t H, const void* table, int32_t dtype, void* out, void* stream);
+
+/* Synchronises the current device and reports whether any tile kernel on it
+ * gave up a bounded wait since the last reset (VTNK_ERR_DEVICE, with the wait's
+ * code in vtnk_last_error()); reset != 0 clears the record.  Diagnostic, not on
+ * the hot path (no reference counterpart: the reference's kernels have no
+ * bounded waits). */
+int vtnk_device_status(int reset);
 
 /* Human-readable description of the last error on this host thread. */
 const char* vtnk_last_error(void);

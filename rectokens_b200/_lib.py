@@ -23,11 +23,13 @@ EXPORTS = (
     "vtnk_fused_linear_constrained_node_transition_topk",
     "vtnk_fused_linear_constrained_node_transition_sampling",
     "vtnk_gumbel_noise",
+    "vtnk_build_child_index",
     "vtnk_beam_step",
     "vtnk_beam_merge",
     "vtnk_beam_search_workspace_bytes",
     "vtnk_beam_search",
     "vtnk_synth_normal",
+    "vtnk_device_status",
     "vtnk_last_error",
     "vtnk_version",
 )
@@ -44,11 +46,16 @@ class Linear(ctypes.Structure):
                 ("b_stride_n", c_int64), ("bias", c_void_p), ("dtype", c_int32)]
 
 
+class ChildIndex(ctypes.Structure):
+    _fields_ = [("masks", c_void_p), ("node_lo", c_int64), ("node_hi", c_int64),
+                ("window_lo", c_int64), ("window_n", c_int64)]
+
+
 class Search(ctypes.Structure):
     _fields_ = [("hidden", POINTER(c_void_p)), ("hidden_stride", c_int64), ("weight", c_void_p),
                 ("n_vocab", c_int64), ("hidden_dim", c_int64), ("bias", c_void_p),
                 ("dtype", c_int32), ("csr", Csr), ("layer_max_branches", POINTER(c_int64)),
-                ("window_lo", POINTER(c_int64)), ("window_n", POINTER(c_int64)),
+                ("index", POINTER(ChildIndex)),
                 ("levels", c_int64), ("batch", c_int64), ("beams", c_int64), ("n_cand", c_int64)]
 
 
@@ -75,7 +82,9 @@ def lib() -> ctypes.CDLL:
             "vtnk_fused_linear_constrained_node_transition_sampling":
                 [POINTER(Linear), P, POINTER(Csr), I64, c_uint64, P, P, P, P, V],
             "vtnk_gumbel_noise": [c_uint64, I64, I64, P, V],
-            "vtnk_beam_step": [POINTER(Linear), P, POINTER(Csr), I64, I64, I64, I64, P, P, P, P, V],
+            "vtnk_build_child_index": [POINTER(Csr), POINTER(ChildIndex), V],
+            "vtnk_beam_step": [POINTER(Linear), P, POINTER(Csr), I64, I64, POINTER(ChildIndex),
+                               P, P, P, P, V],
             "vtnk_beam_merge": [I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, V],
             "vtnk_beam_search": [POINTER(Search), P, c_size_t, P, P, P, V],
             "vtnk_synth_normal": [c_uint64, c_uint64, I64, I64, I64, P, c_int32, P, V],
@@ -86,6 +95,8 @@ def lib() -> ctypes.CDLL:
             fn.restype = c_int
         L.vtnk_beam_search_workspace_bytes.argtypes = [POINTER(Search)]
         L.vtnk_beam_search_workspace_bytes.restype = c_size_t
+        L.vtnk_device_status.argtypes = [c_int]
+        L.vtnk_device_status.restype = c_int
         L.vtnk_last_error.argtypes = []
         L.vtnk_last_error.restype = c_char_p
         L.vtnk_version.argtypes = []

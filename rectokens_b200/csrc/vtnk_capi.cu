@@ -112,12 +112,12 @@ SearchLayout search_layout(const vtnk_search_t* s) {
 
 // One fused level: tcgen05 tile kernel when the shape allows, else rows kernel.
 int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
-                   int64_t mb, int64_t n_cand, int64_t window_lo, int64_t window_n,
+                   int64_t mb, int64_t n_cand, const vtnk_child_index_t* index,
                    int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
                    cudaStream_t s) {
   if (lin->rows == 0) return VTNK_OK;
-  if (tc_enabled() && lin->dtype == VTNK_BF16 && window_n > 0 && window_n <= 256 &&
-      lin->b_stride_k == 1 && lin->rows >= 128) {
+  if (tc_enabled() && index && index->masks && lin->dtype == VTNK_BF16 && lin->b_stride_k == 1 &&
+      lin->rows >= 128) {
     TcArgs t{};
     t.a = lin->a;
     t.rows = lin->rows;
@@ -125,8 +125,12 @@ int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk
     t.a_stride = lin->a_stride;
     t.w = lin->b;
     t.w_stride = lin->b_stride_n;
-    t.window_lo = window_lo;
-    t.window_n = static_cast<int>(window_n);
+    t.n_vocab = lin->n_vocab;
+    t.window_lo = index->window_lo;
+    t.window_n = static_cast<int>(index->window_n);
+    t.masks = index->masks;
+    t.idx_lo = index->node_lo;
+    t.idx_hi = index->node_hi;
     t.bias = lin->bias;
     t.cur_node = cur_node;
     t.csr = make_csr(*csr);
@@ -238,18 +242,33 @@ int vtnk_gumbel_noise(uint64_t seed, int64_t rows, int64_t max_branches, float* 
   return launch_gumbel(seed, rows, max_branches, out, as_stream(stream));
 }
 
+int vtnk_build_child_index(const vtnk_csr_t* csr, const vtnk_child_index_t* index,
+                           void* stream) {
+  int rc = check_csr(csr);
+  if (rc) return rc;
+  VTNK_REQUIRE(index != nullptr, "index is NULL");
+  VTNK_REQUIRE(index->node_lo >= 0 && index->node_hi >= index->node_lo, "bad node range");
+  VTNK_REQUIRE(index->window_n >= 1 && index->window_n <= 256 && index->window_lo >= 0,
+               "window must hold 1..256 tokens");
+  VTNK_REQUIRE(index->node_hi == index->node_lo || index->masks, "masks is NULL");
+  VTNK_REQUIRE((reinterpret_cast<uintptr_t>(index->masks) & 15) == 0,
+               "masks must be 16-byte aligned");
+  return launch_build_child_index(make_csr(*csr), const_cast<uint32_t*>(index->masks),
+                                  index->node_lo, index->node_hi, index->window_lo,
+                                  static_cast<int>(index->window_n), as_stream(stream));
+}
+
 int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
-                   int64_t max_branches, int64_t n_cand, int64_t window_lo, int64_t window_n,
+                   int64_t max_branches, int64_t n_cand, const vtnk_child_index_t* index,
                    int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
                    void* stream) {
   int rc = check_step(lin, csr, max_branches);
   if (rc) return rc;
   VTNK_REQUIRE(n_cand >= 1 && n_cand <= 1024, "n_cand out of range");
-  VTNK_REQUIRE(window_n >= 0, "window_n < 0");
   VTNK_REQUIRE(lin->rows == 0 || (cand_tok && cand_logit && cand_node && row_lse),
                "NULL pointer");
-  return beam_step_impl(lin, cur_node, csr, max_branches, n_cand, window_lo, window_n, cand_tok,
-                        cand_logit, cand_node, row_lse, as_stream(stream));
+  return beam_step_impl(lin, cur_node, csr, max_branches, n_cand, index, cand_tok, cand_logit,
+                        cand_node, row_lse, as_stream(stream));
 }
 
 int vtnk_beam_merge(int64_t level, int64_t B, int64_t k, int64_t n_cand,
@@ -327,9 +346,8 @@ int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_b
     lin.dtype = s->dtype;
     rc = check_linear(&lin);
     if (rc) return rc;
-    const int64_t wlo = s->window_lo ? s->window_lo[level] : 0;
-    const int64_t wn = s->window_n ? s->window_n[level] : 0;
-    rc = beam_step_impl(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand, wlo, wn,
+    const vtnk_child_index_t* idx = s->index ? &s->index[level] : nullptr;
+    rc = beam_step_impl(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand, idx,
                         cand_tok, cand_logit, cand_node, lse, st);
     if (rc) return rc;
     const bool last = level + 1 == s->levels;
@@ -343,6 +361,19 @@ int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_b
     prev_node = node;
     prev_logp = logp;
     prev_ids = ids;
+  }
+  return VTNK_OK;
+}
+
+int vtnk_device_status(int reset) {
+  const cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "device synchronize");
+  int v = 0;
+  const int rc = read_tc_status(&v, reset != 0);
+  if (rc) return rc;
+  if (v != 0) {
+    set_error("a tile kernel's bounded wait expired (code %d)", v);
+    return VTNK_ERR_DEVICE;
   }
   return VTNK_OK;
 }

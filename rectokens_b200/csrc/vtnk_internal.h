@@ -55,8 +55,11 @@ struct TcArgs {
   int64_t rows, H, a_stride;
   const void* w;            // bf16 W rows [N, H] (row stride w_stride), window rows used
   int64_t w_stride;
+  int64_t n_vocab;          // rows of W
   int64_t window_lo;        // first token of the column window
   int window_n;             // <= 256
+  const uint32_t* masks;    // child-bitmask index [idx_hi - idx_lo, 8]
+  int64_t idx_lo, idx_hi;
   const void* bias;         // bf16 [N] or nullptr
   const int64_t* cur_node;  // nullptr: root
   Csr csr;
@@ -66,7 +69,6 @@ struct TcArgs {
   float* cand_logit;
   int64_t* cand_node;
   float* row_lse;
-  int* status;              // device word: 0 ok, else a failure code
 };
 
 int launch_rows(const RowsArgs& p, int mode, int dtype, cudaStream_t s);
@@ -82,5 +84,9 @@ int launch_gumbel(uint64_t seed, int64_t rows, int64_t mb, float* out, cudaStrea
 // fit the tile kernel; the caller then uses the row kernel.
 int launch_beam_step_tc(const TcArgs& p, cudaStream_t s);
 bool tc_enabled();
+int launch_build_child_index(const Csr& csr, uint32_t* masks, int64_t node_lo, int64_t node_hi,
+                             int64_t window_lo, int window_n, cudaStream_t s);
+// Reads (and optionally clears) the tile kernel's device status word.
+int read_tc_status(int* out, bool reset);
 
 }  // namespace vtnk

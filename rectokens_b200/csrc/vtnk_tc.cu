@@ -1,11 +1,669 @@
-// Tensor-core beam step (tcgen05 / TMEM / TMA) -- placeholder until the tile
-// kernel lands: every call reports "unsupported" so the row kernel runs.
+// Tensor-core beam step for sm_100a: tcgen05.mma with TMEM accumulators fed
+// by TMA, fused with the trie child mask, per-row top-n, log-sum-exp and the
+// next-node lookup.  Full logits never leave the SM.
+//
+// Per level the contraction is a dense GEMM  D[R, 256] = A[R, H] . Wwin[256, H]^T
+// where Wwin = the LM-head rows of the level's token window (every child of
+// every node at this depth lies in [window_lo, window_lo + 256)).  Columns
+// that are not children of a row's node are dropped in the epilogue, using
+// the depth's child-bitmask index (32 bytes per node, built once per trie).
+//
+// CTA layout (persistent, one CTA per SM, 192 threads):
+//   warp 0      TMA producer      A tile [128 x 64] + W tile [256 x 64] per stage
+//   warp 1      MMA issuer        tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16
+//                                 (also allocates / frees 512 TMEM columns)
+//   warps 2..5  epilogue          thread = row: tcgen05.ld 32x32b, mask, top-n, LSE
+// Shared memory: 4 stages x 48 KB operand ring (SWIZZLE_128B, K-major), the
+// window's bias, mbarriers.  TMEM holds two 128 x 256 fp32 accumulators so
+// the epilogue of tile i overlaps the MMAs of tile i + 1.
+//
+// Every mbarrier wait is bounded in time; on expiry the CTA records a status
+// code in a device word (read by vtnk_device_status), drains its in-flight
+// copies and MMAs with bounded waits, frees its TMEM and exits.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <climits>
+#include <cstdlib>
+#include <mutex>
+
 #include "vtnk_internal.h"
 
 namespace vtnk {
 
-bool tc_enabled() { return false; }
+__device__ int g_tc_status = 0;  // 0 ok; else the first failing wait's code
 
-int launch_beam_step_tc(const TcArgs&, cudaStream_t) { return VTNK_ERR_UNSUPPORTED; }
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;
+constexpr int B_BYTES = BN * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = (2 + EPI_WARPS) * 32;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
+
+struct Shared {
+  uint8_t ring[STAGES][STAGE_BYTES];  // 1024-aligned stages
+  float bias[BN];
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
+
+struct Params {
+  int64_t rows, H;
+  const int64_t* cur_node;
+  Csr csr;
+  int64_t mb;
+  int64_t window_lo;
+  int window_n;
+  int n_cand;
+  const uint32_t* masks;
+  int64_t idx_lo, idx_hi;
+  const __nv_bfloat16* a;
+  int64_t a_stride;
+  const __nv_bfloat16* w;
+  int64_t w_stride;
+  const __nv_bfloat16* bias;
+  int64_t n_vocab;
+  int64_t* cand_tok;
+  float* cand_logit;
+  int64_t* cand_node;
+  float* row_lse;
+};
+
+// ------------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ uint32_t su32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ uint64_t gtimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Wait for phase `parity` of barrier b; false when the CTA is aborting or the
+// time limit ran out (then the abort flag and the device status are set).
+__device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatile int* abort,
+                                           int code) {
+  if (mbar_try_wait(b, parity)) return true;
+  const uint64_t t0 = gtimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((i & 31) == 0) {
+      if (*abort) return false;
+      if (gtimer() - t0 > WAIT_LIMIT_NS || i > (1u << 30)) {
+        *abort = 1;
+        atomicCAS(&g_tc_status, 0, code);
+        return false;
+      }
+    }
+  }
+}
+// Drain wait at teardown: bounded, never sets abort.
+__device__ __forceinline__ void drain_phase(uint64_t* b, uint32_t parity) {
+  const uint64_t t0 = gtimer();
+  while (!mbar_try_wait(b, parity))
+    if (gtimer() - t0 > WAIT_LIMIT_NS / 4) return;
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major operand in the 128-byte swizzle
+// layout TMA writes (8-row x 128-byte atoms, 1024 B between atoms).
+__device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem) {
+  const uint64_t addr = su32(smem);
+  return ((addr & 0x3FFFF) >> 4)                      // start address (16 B units)
+         | (1ull << 16)                               // leading byte offset (unused here)
+         | (static_cast<uint64_t>(1024 >> 4) << 32)   // stride byte offset: 8 rows x 128 B
+         | (1ull << 46)                               // descriptor version (sm_100)
+         | (2ull << 61);                              // layout: SWIZZLE_128B
+}
+// Instruction descriptor: kind::f16, A = B = bf16, D = fp32, both K-major,
+// N = 256, M = 128.
+constexpr uint32_t IDESC =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((BM >> 4) << 24);
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(da), "l"(db), "r"(IDESC), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          su32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]),
+        "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]),
+        "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// ------------------------------------------------------------------ per-row selection
+template <int NC>
+struct TopN {
+  float v[NC];
+  int c[NC];
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      v[i] = -INFINITY;
+      c[i] = -1;
+    }
+  }
+  // Larger value first; an equal value never displaces an earlier entry, so
+  // feeding columns in increasing order breaks ties toward the lower column.
+  __device__ __forceinline__ void push(float x, int col) {
+    if (!(x > v[NC - 1])) return;
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      if (x > v[i]) {
+        const float tv = v[i];
+        const int tc = c[i];
+        v[i] = x;
+        c[i] = col;
+        x = tv;
+        col = tc;
+      }
+    }
+  }
+};
+
+// Exact per-row path for a row whose node is outside the index or whose
+// children are not a clean sorted in-window set (slow, never taken for a
+// sorted catalog trie queried at the right depth).
+template <int NC>
+__device__ void row_scalar(const Params& p, int64_t row, int64_t start, int count, TopN<NC>& t,
+                           float& lse) {
+  const __nv_bfloat16* ar = p.a + row * p.a_stride;
+  float m = -INFINITY, s = 0.f;
+  for (int j = 0; j < count; ++j) {
+    const int64_t col = __ldg(p.csr.cols + start + j);
+    if (col < 0 || col >= p.n_vocab) continue;
+    const __nv_bfloat16* wr = p.w + col * p.w_stride;
+    float acc = 0.f;
+    for (int64_t h = 0; h < p.H; ++h)
+      acc = fmaf(__bfloat162float(ar[h]), __bfloat162float(wr[h]), acc);
+    if (p.bias) acc += __bfloat162float(p.bias[col]);
+    if (acc > m) {
+      s = s * __expf(m - acc) + 1.f;
+      m = acc;
+    } else {
+      s += __expf(acc - m);
+    }
+    t.push(acc, j);  // slot index; mapped to token / node by the caller
+  }
+  lse = (m > -INFINITY) ? m + __logf(s) : -INFINITY;
+}
+
+template <int NC>
+__global__ void __launch_bounds__(THREADS, 1)
+beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                 const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  Shared& S = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                         ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t n_tiles = (p.rows + BM - 1) / BM;
+  const int kblocks = static_cast<int>((p.H + BK - 1) / BK);
+  volatile int* abort = &S.abort;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&S.tfull[b], 1);
+      mbar_init(&S.tempty[b], EPI_WARPS);
+    }
+    mbar_init(&S.mma_done, 1);
+    S.abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     su32(&S.tmem_base)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  for (int i = threadIdx.x; i < BN; i += THREADS) {
+    const int64_t col = p.window_lo + i;
+    S.bias[i] =
+        (p.bias && i < p.window_n && col < p.n_vocab) ? __bfloat162float(p.bias[col]) : 0.f;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = S.tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (lane == 0) {
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+      uint32_t armed[STAGES] = {0, 0, 0, 0};
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_phase(&S.empty[stage], phase ^ 1, abort, 1)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = S.ring[stage];
+          mbar_expect_tx(&S.full[stage], STAGE_BYTES);
+          tma_load_2d(st, &tmA, &S.full[stage], kb * BK, static_cast<int>(tile * BM));
+          tma_load_2d(st + A_BYTES, &tmW, &S.full[stage], kb * BK, static_cast<int>(p.window_lo));
+          ++armed[stage];
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // copies still in flight land before the CTA exits
+      for (int s = 0; s < STAGES; ++s)
+        if (armed[s]) drain_phase(&S.full[s], (armed[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t it = 0;
+      bool ok = true;
+      for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+        const uint32_t buf = it & 1;
+        if (!wait_phase(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + buf * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!wait_phase(&S.full[stage], phase, abort, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = umma_desc_sw128(S.ring[stage]);
+          const uint64_t db = umma_desc_sw128(S.ring[stage] + A_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)  // +32 B per K=16 step inside the swizzle atom
+            umma_bf16(d, da + 2 * k, db + 2 * k, (kb | k) != 0);
+          umma_commit(&S.empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) umma_commit(&S.tfull[buf]);
+      }
+      umma_commit(&S.mma_done);
+      drain_phase(&S.mma_done, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int lg = warp & 3;             // TMEM lane group this warp may access
+    const int r_local = lg * 32 + lane;  // row within the tile == TMEM lane
+    uint32_t it = 0;
+    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      const int64_t row = tile * BM + r_local;
+      const bool live = row < p.rows;
+      // The row's children as a 256-bit mask over the window, read from the
+      // depth's child index (two 16-byte loads).  A row whose node is outside
+      // the index, or whose mask does not hold exactly its `count` children
+      // (unsorted / out-of-window children, or more than max_branches), takes
+      // the exact per-row path.
+      int64_t start = 0;
+      int count = 0;
+      uint32_t m[BN / 32];
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) m[i] = 0u;
+      int spill = 0;
+      if (live) {
+        const int64_t cur = p.cur_node ? __ldg(p.cur_node + row) : 0;
+        node_children(p.csr, cur, p.mb, start, count);
+        if (cur >= p.idx_lo && cur < p.idx_hi) {
+          const uint4* q = reinterpret_cast<const uint4*>(p.masks + (cur - p.idx_lo) * (BN / 32));
+          const uint4 x = __ldg(q), y = __ldg(q + 1);
+          m[0] = x.x; m[1] = x.y; m[2] = x.z; m[3] = x.w;
+          m[4] = y.x; m[5] = y.y; m[6] = y.z; m[7] = y.w;
+        }
+        int pc = 0;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) pc += __popc(m[i]);
+        spill = pc != count;
+      }
+
+      const uint32_t buf = it & 1;
+      const bool ok = wait_phase(&S.tfull[buf], (it >> 1) & 1, abort, 4);
+      __syncwarp();
+      if (__any_sync(0xffffffffu, !ok)) break;
+      tc_fence_after();
+
+      TopN<NC> top;
+      top.init();
+      float mx = -INFINITY, sum = 0.f;
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BN;
+#pragma unroll 1
+      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+        uint32_t v[32];
+        __syncwarp();
+        tmem_ld32(taddr + chunk * 32, v);  // warp-collective: every lane, every chunk
+        uint32_t mw = 0;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) mw = (i == chunk) ? m[i] : mw;
+        float cm = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = __uint_as_float(v[i]) + S.bias[chunk * 32 + i];
+          v[i] = __float_as_uint(x);
+          if ((mw >> i) & 1u) cm = fmaxf(cm, x);
+        }
+        if (cm > mx) {
+          sum *= __expf(mx - cm);
+          mx = cm;
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if ((mw >> i) & 1u) {
+            const float x = __uint_as_float(v[i]);
+            sum += __expf(x - mx);
+            top.push(x, chunk * 32 + i);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.tempty[buf]);
+
+      float lse = (mx > -INFINITY) ? mx + __logf(sum) : -INFINITY;
+      bool by_slot = false;
+      if (spill && live) {  // exact scalar recompute of this row
+        top.init();
+        row_scalar<NC>(p, row, start, count, top, lse);
+        by_slot = true;
+      }
+      if (live) {
+        int pre[BN / 32];
+        int acc = 0;
+#pragma unroll
+        for (int i = 0; i < BN / 32; ++i) {
+          pre[i] = acc;
+          acc += __popc(m[i]);
+        }
+        int64_t* ot = p.cand_tok + row * p.n_cand;
+        float* ol = p.cand_logit + row * p.n_cand;
+        int64_t* on = p.cand_node + row * p.n_cand;
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+          if (j >= p.n_cand) break;
+          const int c = top.c[j];
+          int64_t tok = -1, node = -1;
+          float lv = -INFINITY;
+          if (c >= 0) {
+            int slot;
+            if (by_slot) {
+              slot = c;
+              tok = __ldg(p.csr.cols + start + slot);
+            } else {
+              const int wi = c >> 5;
+              int base = 0;
+              uint32_t word = 0;
+#pragma unroll
+              for (int i = 0; i < BN / 32; ++i) {
+                base = (i == wi) ? pre[i] : base;
+                word = (i == wi) ? m[i] : word;
+              }
+              slot = base + __popc(word & ((1u << (c & 31)) - 1u));
+              tok = p.window_lo + c;
+            }
+            node = __ldg(p.csr.vals + start + slot);
+            lv = top.v[j];
+          }
+          ot[j] = tok;
+          ol[j] = lv;
+          on[j] = node;
+        }
+        p.row_lse[row] = lse;
+      }
+    }
+  }
+
+  // ------------------------------------------------------------------ teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+// Child-bitmask index: one warp per node.  Bits for children inside the
+// window; an all-zero mask when a child is outside it or out of order.
+__global__ void build_index_kernel(const Csr csr, uint32_t* __restrict__ masks, int64_t node_lo,
+                                   int64_t node_hi, int64_t window_lo, int window_n) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t node = node_lo + static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) +
+                      (threadIdx.x >> 5);
+       node < node_hi; node += warps) {
+    int64_t start;
+    int count;
+    node_children(csr, node, INT32_MAX, start, count);
+    uint32_t word[BN / 32];
+#pragma unroll
+    for (int i = 0; i < BN / 32; ++i) word[i] = 0u;
+    int bad = 0;
+    int64_t carry = INT64_MIN;
+    for (int j0 = 0; j0 < count; j0 += 32) {
+      const int j = j0 + lane;
+      const bool has = j < count;
+      const int64_t t = has ? __ldg(csr.cols + start + j) - window_lo : INT64_MAX;
+      int64_t tp = __shfl_up_sync(0xffffffffu, t, 1);
+      if (lane == 0) tp = carry;
+      carry = __shfl_sync(0xffffffffu, t, 31);
+      const bool inwin = has && t >= 0 && t < window_n;
+      if (has && (!inwin || t <= tp)) bad = 1;
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) {
+        const uint32_t bit = (inwin && (t >> 5) == i) ? (1u << (t & 31)) : 0u;
+        word[i] |= __reduce_or_sync(0xffffffffu, bit);
+      }
+    }
+    bad = __any_sync(0xffffffffu, bad);
+    if (lane < BN / 32) {
+      uint32_t w = 0;
+#pragma unroll
+      for (int i = 0; i < BN / 32; ++i) w = (i == lane) ? word[i] : w;
+      masks[(node - node_lo) * (BN / 32) + lane] = bad ? 0u : w;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host side
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* f = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  return fn;
+}
+
+bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+            es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int sm_count() {
+  int dev = 0, n = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n;
+}
+
+template <int NC>
+int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, cudaStream_t s) {
+  auto k = beam_step_kernel<NC>;
+  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       static_cast<int>(SMEM_BYTES));
+  const int64_t tiles = (p.rows + BM - 1) / BM;
+  const int sms = sm_count();
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  k<<<grid, THREADS, SMEM_BYTES, s>>>(a, w, p);
+  return cuda_status(cudaGetLastError(), "beam_step_tc launch");
+}
+
+}  // namespace tc
+
+bool tc_enabled() {
+  static int enabled = -1;
+  if (enabled < 0) {
+    const char* e = getenv("VTNK_DISABLE_TC");
+    enabled = (e && e[0] == '1') ? 0 : 1;
+  }
+  return enabled == 1;
+}
+
+int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
+  using namespace tc;
+  auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (!t.masks || !aligned(t.masks) || t.idx_hi < t.idx_lo || t.window_n < 1 ||
+      t.window_n > BN || t.n_cand < 1 || t.n_cand > 32 || t.rows < 1 || t.H % 8 != 0 ||
+      t.a_stride % 8 != 0 || t.w_stride % 8 != 0 || !aligned(t.a) || !aligned(t.w) || t.mb < 1 ||
+      t.window_lo < 0 || t.rows > (int64_t(1) << 31) - BM)
+    return VTNK_ERR_UNSUPPORTED;
+  Params p{};
+  p.rows = t.rows;
+  p.H = t.H;
+  p.cur_node = t.cur_node;
+  p.csr = t.csr;
+  p.mb = t.mb;
+  p.window_lo = t.window_lo;
+  p.window_n = t.window_n;
+  p.n_cand = t.n_cand;
+  p.masks = t.masks;
+  p.idx_lo = t.idx_lo;
+  p.idx_hi = t.idx_hi;
+  p.a = static_cast<const __nv_bfloat16*>(t.a);
+  p.a_stride = t.a_stride;
+  p.w = static_cast<const __nv_bfloat16*>(t.w);
+  p.w_stride = t.w_stride;
+  p.bias = static_cast<const __nv_bfloat16*>(t.bias);
+  p.n_vocab = t.n_vocab;
+  p.cand_tok = t.cand_tok;
+  p.cand_logit = t.cand_logit;
+  p.cand_node = t.cand_node;
+  p.row_lse = t.row_lse;
+  CUtensorMap ma, mw;
+  if (!make_map(&ma, t.a, t.H, t.rows, t.a_stride * 2, BK, BM) ||
+      !make_map(&mw, t.w, t.H, t.n_vocab, t.w_stride * 2, BK, BN)) {
+    set_error("cuTensorMapEncodeTiled failed");
+    return VTNK_ERR_CUDA;
+  }
+  if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, s);
+  if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, s);
+  if (t.n_cand <= 16) return launch_nc<16>(ma, mw, p, s);
+  return launch_nc<32>(ma, mw, p, s);
+}
+
+int launch_build_child_index(const Csr& csr, uint32_t* masks, int64_t node_lo, int64_t node_hi,
+                             int64_t window_lo, int window_n, cudaStream_t s) {
+  if (node_hi <= node_lo) return VTNK_OK;
+  const int64_t warps = node_hi - node_lo;
+  int64_t blocks = (warps + 7) / 8;
+  if (blocks > 148 * 32) blocks = 148 * 32;
+  tc::build_index_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(csr, masks, node_lo, node_hi,
+                                                                  window_lo, window_n);
+  return cuda_status(cudaGetLastError(), "build_index_kernel launch");
+}
+
+int read_tc_status(int* out, bool reset) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_status(e, "read device status");
+  if (reset && v != 0) {
+    const int z = 0;
+    e = cudaMemcpyToSymbol(g_tc_status, &z, sizeof(int));
+    if (e != cudaSuccess) return cuda_status(e, "reset device status");
+  }
+  *out = v;
+  return VTNK_OK;
+}
 
 }  // namespace vtnk

@@ -18,6 +18,7 @@ children, and ``dense_states`` maps them to the same node ids
 from __future__ import annotations
 
 import ctypes
+import weakref
 from typing import NamedTuple, Sequence
 
 import torch
@@ -34,23 +35,43 @@ class BeamSearchResult(NamedTuple):
     cur_node: Tensor        # (B * k,) int64 trie node reached
 
 
-# ------------------------------------------------------------------ level windows
-_WINDOW_CACHE: dict = {}
+# ------------------------------------------------------------------ per-depth layout
+class DepthLayout(NamedTuple):
+    node_lo: int    # nodes of this depth are [node_lo, node_hi) (BFS order)
+    node_hi: int
+    window_lo: int  # every child token of those nodes lies in [window_lo, window_lo + window_n)
+    window_n: int
 
 
-def level_windows(trie: CompactCSRTrie) -> list[tuple[int, int]]:
-    """Token range ``(lo, n)`` holding every child of every node at each depth.
+_LAYOUT_CACHE: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+
+
+def _cache_slot(trie: CompactCSRTrie) -> dict:
+    """Per-trie cache, held weakly by the trie's row_ptrs tensor and keyed by
+    both arrays' identity and version counters (an in-place edit or a new
+    array invalidates it; the cached entry keeps the arrays it was built
+    from alive, so their memory cannot be reused under it)."""
+    per = _LAYOUT_CACHE.setdefault(trie.row_ptrs, {})
+    key = (id(trie.stacked_cols_vals), trie.stacked_cols_vals._version, trie.row_ptrs._version)
+    slot = per.get(key)
+    if slot is None:
+        per.clear()
+        slot = per[key] = {"cols_vals": trie.stacked_cols_vals}
+    return slot
+
+
+def depth_layout(trie: CompactCSRTrie) -> list[DepthLayout]:
+    """Node range and child-token window of every depth.
 
     Nodes are numbered in BFS order, so the nodes of one depth -- and the edges
     leaving them -- are contiguous; the window of depth ``d`` is the min/max
-    child token over that edge range.  Computed once per trie storage (a few
-    host synchronisations) and cached.
+    child token over that edge range.  Computed once per trie (a few host
+    synchronisations) and cached.
     """
+    slot = _cache_slot(trie)
+    if "layout" in slot:
+        return slot["layout"]
     rp, cv = trie.row_ptrs, trie.stacked_cols_vals
-    key = (rp.data_ptr(), cv.data_ptr(), rp.numel(), cv.shape[1], str(rp.device))
-    hit = _WINDOW_CACHE.get(key)
-    if hit is not None:
-        return hit
     n_nodes, nnz = rp.numel(), cv.shape[1] - 1
     out = []
     n0, n1 = 0, 1
@@ -58,17 +79,47 @@ def level_windows(trie: CompactCSRTrie) -> list[tuple[int, int]]:
         e0 = int(rp[n0]) if n0 < n_nodes else nnz
         e1 = int(rp[n1]) if n1 < n_nodes else nnz
         if e1 <= e0:
-            out.append((0, 0))
-            n0, n1 = n1, n1
+            out.append(DepthLayout(n0, n1, 0, 0))
+            n0 = n1
             continue
         seg = cv[0, e0:e1]
         lo, hi = int(seg.min()), int(seg.max())
-        out.append((lo, hi - lo + 1))
+        out.append(DepthLayout(n0, n1, lo, hi - lo + 1))
         n0, n1 = e0 + 1, e1 + 1
-    if len(_WINDOW_CACHE) > 64:
-        _WINDOW_CACHE.clear()
-    _WINDOW_CACHE[key] = out
+    slot["layout"] = out
     return out
+
+
+def level_windows(trie: CompactCSRTrie) -> list[tuple[int, int]]:
+    """``(window_lo, window_n)`` of every depth (see ``depth_layout``)."""
+    return [(d.window_lo, d.window_n) for d in depth_layout(trie)]
+
+
+def child_index(trie: CompactCSRTrie, depth: int):
+    """The depth's child-bitmask index (``_lib.ChildIndex``, or ``None`` when
+    the depth's window is wider than one 256-column tile).  Built on the
+    trie's device on first use and cached with the trie."""
+    slot = _cache_slot(trie)
+    idx = slot.setdefault("index", {})
+    if depth in idx:
+        return idx[depth][0]
+    d = depth_layout(trie)[depth]
+    if not 1 <= d.window_n <= 256 or trie.row_ptrs.device.type != "cuda":
+        idx[depth] = (None, None)
+        return None
+    masks = torch.empty((max(1, d.node_hi - d.node_lo), 8), dtype=torch.int32,
+                        device=trie.row_ptrs.device)
+    ci = L.ChildIndex(masks.data_ptr(), d.node_lo, d.node_hi, d.window_lo, d.window_n)
+    csr = L.csr_struct(trie.row_ptrs, trie.stacked_cols_vals)
+    L.check(L.lib().vtnk_build_child_index(csr, ci, L.stream_of(masks.device)))
+    idx[depth] = (ci, masks)
+    return ci
+
+
+def child_index_masks(trie: CompactCSRTrie, depth: int):
+    """The mask tensor ``(nodes, 8)`` int32 behind ``child_index`` (or None)."""
+    child_index(trie, depth)
+    return _cache_slot(trie)["index"][depth][1]
 
 
 # ------------------------------------------------------------------ workspace
@@ -84,7 +135,7 @@ def _workspace(device: torch.device, nbytes: int) -> Tensor:
 
 
 def _search_struct(hidden: Sequence[Tensor], weight: Tensor, bias, trie: CompactCSRTrie,
-                   beams: int, n_cand: int, windows, keep: list):
+                   beams: int, n_cand: int, use_index: bool, keep: list):
     levels = len(hidden)
     if levels < 1:
         raise ValueError("need at least one level")
@@ -101,15 +152,17 @@ def _search_struct(hidden: Sequence[Tensor], weight: Tensor, bias, trie: Compact
         raise ValueError("weight must be a contiguous (N, H) tensor")
     hp = (ctypes.c_void_p * levels)(*[h.data_ptr() for h in hidden])
     mb = (ctypes.c_int64 * levels)(*trie.layer_max_branches[:levels])
-    wlo = (ctypes.c_int64 * levels)(*[w[0] for w in windows[:levels]])
-    wn = (ctypes.c_int64 * levels)(*[w[1] for w in windows[:levels]])
-    keep += [hp, mb, wlo, wn]
+    idx = (L.ChildIndex * levels)()
+    for l in range(levels):
+        ci = child_index(trie, l) if use_index else None
+        if ci is not None:
+            idx[l] = ci
+    keep += [hp, mb, idx]
     csr = L.csr_struct(trie.row_ptrs, trie.stacked_cols_vals)
     return L.Search(ctypes.cast(hp, ctypes.POINTER(ctypes.c_void_p)), H, weight.data_ptr(),
                     weight.shape[0], H, L.ptr(bias), L.DTYPE_CODE[dt], csr,
                     ctypes.cast(mb, ctypes.POINTER(ctypes.c_int64)),
-                    ctypes.cast(wlo, ctypes.POINTER(ctypes.c_int64)),
-                    ctypes.cast(wn, ctypes.POINTER(ctypes.c_int64)),
+                    ctypes.cast(idx, ctypes.POINTER(L.ChildIndex)),
                     levels, B, beams, n_cand)
 
 
@@ -119,7 +172,7 @@ def constrained_beam_search(
     trie: CompactCSRTrie,
     config: GenerationConfig,
     bias: Tensor | None = None,
-    use_windows: bool = True,
+    use_index: bool = True,
 ) -> BeamSearchResult:
     """Run an ``L = len(hidden)``-level beam search on the GPU in one call.
 
@@ -134,9 +187,8 @@ def constrained_beam_search(
     dev = weight.device
     if dev.type != "cuda":
         raise RuntimeError("constrained_beam_search runs on CUDA tensors only")
-    windows = level_windows(trie) if use_windows else [(0, 0)] * len(hidden)
     keep: list = []
-    s = _search_struct(hidden, weight, bias, trie, config.k, config.beam_size, windows, keep)
+    s = _search_struct(hidden, weight, bias, trie, config.k, config.beam_size, use_index, keep)
     B, k, Lv = s.batch, s.beams, s.levels
     lib = L.lib()
     nbytes = lib.vtnk_beam_search_workspace_bytes(s)
@@ -150,21 +202,23 @@ def constrained_beam_search(
 
 
 def beam_step(a: Tensor, weight: Tensor, trie: CompactCSRTrie, step: int, cur_node: Tensor | None,
-              n_cand: int, bias: Tensor | None = None, window: tuple[int, int] | None = None):
+              n_cand: int, bias: Tensor | None = None, index="auto"):
     """One fused level: ``(cand_tok, cand_logit, cand_node, row_lse)`` for the
-    rows of ``a`` at trie depth ``step`` (``cur_node=None``: the root)."""
+    rows of ``a`` at trie depth ``step`` (``cur_node=None``: the root).
+    ``index``: ``"auto"`` (the depth's cached child index), ``None`` (CUDA-core
+    row kernel) or an explicit ``_lib.ChildIndex``."""
     dev = a.device
     R = a.shape[0]
     mb = trie.layer_max_branches[step]
-    if window is None:
-        window = level_windows(trie)[step]
+    if isinstance(index, str):
+        index = child_index(trie, step)
     tok = torch.empty((R, n_cand), dtype=torch.int64, device=dev)
     logit = torch.empty((R, n_cand), dtype=torch.float32, device=dev)
     node = torch.empty((R, n_cand), dtype=torch.int64, device=dev)
     lse = torch.empty((R,), dtype=torch.float32, device=dev)
     lin = L.linear_struct(a, weight.T, bias)
     csr = L.csr_struct(trie.row_ptrs, trie.stacked_cols_vals)
-    L.check(L.lib().vtnk_beam_step(lin, L.ptr(cur_node), csr, mb, n_cand, window[0], window[1],
+    L.check(L.lib().vtnk_beam_step(lin, L.ptr(cur_node), csr, mb, n_cand, index,
                                    tok.data_ptr(), logit.data_ptr(), node.data_ptr(),
                                    lse.data_ptr(), L.stream_of(dev)))
     return tok, logit, node, lse
@@ -207,7 +261,6 @@ def constrained_beam_search_from_host(
     copy = torch.cuda.Stream(dev)
     Lv = len(hidden_host)
     B, k = hidden_host[0].shape[0], config.k
-    windows = level_windows(trie)
     dev_h: list = [None] * Lv
     ready: list = [None] * Lv
 
@@ -225,7 +278,7 @@ def constrained_beam_search_from_host(
             issue(l + 1)
         main.wait_event(ready[l])
         dev_h[l].record_stream(main)
-        cand = beam_step(dev_h[l], weight, trie, l, cur, config.beam_size, bias, windows[l])
+        cand = beam_step(dev_h[l], weight, trie, l, cur, config.beam_size, bias)
         prev_ids, prev_logp, cur, _ = beam_merge(l, B, k, cand, prev_logp, prev_ids)
         dev_h[l] = None
     if out is None:

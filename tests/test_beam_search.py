@@ -87,12 +87,11 @@ def _level_by_level(w, n_queries, tol):
     cv = trie.stacked_cols_vals.cpu().numpy()
     W64 = dw.weight.double().cpu().numpy()
     B, k = n_queries, w.beams
-    wins = level_windows(trie)
     prev_logp = prev_ids = cur = None
     for level in range(w.levels):
         rows = B if level == 0 else B * k
         h = dw.hidden[level][:rows]
-        cand = beam_step(h, dw.weight, trie, level, cur, w.topk, window=wins[level])
+        cand = beam_step(h, dw.weight, trie, level, cur, w.topk)
         tok, logit, node, lse = (t.cpu().numpy() for t in cand)
         cur_np = np.zeros(rows, np.int64) if cur is None else cur.cpu().numpy()
         otok, ologit, onode, olp, olse = O.beam_step(
@@ -145,3 +144,95 @@ def test_search_properties_cfg3(cuda_ok):
             assert j.size == 1
             n = cv[1, s + j[0]]
         assert n == res.cur_node[r].item()
+
+
+# --------------------------------------------------------------------- tile kernel
+def _device_status_ok():
+    from rectokens_b200 import _lib as L
+
+    L.check(L.lib().vtnk_device_status(1))
+
+
+def _compare_steps(c1, c2, tol=2e-3):
+    t1, l1, n1, s1 = (x.cpu().numpy() for x in c1)
+    t2, l2, n2, s2 = (x.cpu().numpy() for x in c2)
+    np.testing.assert_allclose(s1, s2, atol=tol, rtol=0)
+    np.testing.assert_allclose(l1, l2, atol=tol, rtol=0)
+    _check_selection(t1, t2, l1, l2)
+    same = t1 == t2
+    np.testing.assert_array_equal(n1[same], n2[same])
+    return same.mean()
+
+
+@pytest.mark.parametrize("n_cand", [1, 4, 10, 20, 32])
+def test_tile_kernel_matches_row_kernel(n_cand, cuda_ok):
+    """The tcgen05 tile path (child index given) against the CUDA-core row
+    path (no index) on the same inputs, every depth of the cfg3 catalog,
+    with a bias and a partial last tile."""
+    w = S.WORKLOADS["cfg3"]
+    dw = WL.make_device_workload(w, DEV)
+    g = torch.Generator(device=DEV).manual_seed(n_cand)
+    bias = (torch.randn(w.vocab, generator=g, device=DEV) * 0.5).to(torch.bfloat16)
+    cur = None
+    for level in range(w.levels):
+        R = 1000 + 37 * level
+        h = dw.hidden[level][:R]
+        tile = beam_step(h, dw.weight, dw.trie, level, cur, n_cand, bias=bias)
+        rows = beam_step(h, dw.weight, dw.trie, level, cur, n_cand, bias=bias, index=None)
+        assert _compare_steps(tile, rows) > 0.99
+        # next depth: each row's best child, tiled to the next level's row count
+        nxt = rows[2][:, 0]
+        cur = nxt.repeat((1000 + 37 * (level + 1)) // nxt.numel() + 1)[: 1000 + 37 * (level + 1)]
+    _device_status_ok()
+
+
+def test_tile_kernel_exact_fallback_rows(cuda_ok):
+    """Rows whose children fall outside the index's window, or are not in
+    ascending token order, are computed exactly by the per-row path."""
+    from rectokens_b200 import _lib as L
+    from rectokens_b200.decoding.beam_search import depth_layout
+
+    w = S.WORKLOADS["cfg2"]
+    dw = WL.make_device_workload(w, DEV)
+    h = dw.hidden[1][:300]
+    cur = torch.arange(1, 301, device=DEV) % 200 + 1       # depth-1 nodes
+    ref = beam_step(h, dw.weight, dw.trie, 1, cur, 10, index=None)
+    d = depth_layout(dw.trie)[1]
+    masks = torch.empty((d.node_hi - d.node_lo, 8), dtype=torch.int32, device=DEV)
+    narrow = L.ChildIndex(masks.data_ptr(), d.node_lo, d.node_hi, d.window_lo + 64, 128)
+    L.check(L.lib().vtnk_build_child_index(
+        L.csr_struct(dw.trie.row_ptrs, dw.trie.stacked_cols_vals), narrow, None))
+    got = beam_step(h, dw.weight, dw.trie, 1, cur, 10, index=narrow)
+    assert _compare_steps(got, ref) > 0.99
+    # reversed child order inside the queried nodes (still a valid CSR trie)
+    rp = dw.trie.row_ptrs
+    cv = dw.trie.stacked_cols_vals.clone()
+    starts, ends = rp[cur].cpu().numpy(), rp[cur + 1].cpu().numpy()
+    for s0, e0 in set(zip(starts.tolist(), ends.tolist())):
+        cv[:, s0:e0] = cv[:, s0:e0].flip(1)
+    rev = dw.trie._replace(stacked_cols_vals=cv)
+    got = beam_step(h, dw.weight, rev, 1, cur, 10)
+    want = beam_step(h, dw.weight, rev, 1, cur, 10, index=None)
+    assert _compare_steps(got, want) > 0.99
+    _device_status_ok()
+
+
+def test_child_index_matches_csr(cuda_ok):
+    """The child-bitmask index holds exactly each node's children (cfg2, every depth)."""
+    from rectokens_b200.decoding.beam_search import child_index, child_index_masks, depth_layout
+
+    w = S.WORKLOADS["cfg2"]
+    dw = WL.make_device_workload(w, DEV)
+    rp = dw.trie.row_ptrs.cpu().numpy()
+    cv = dw.trie.stacked_cols_vals.cpu().numpy()
+    nnz = cv.shape[1] - 1
+    for depth, d in enumerate(depth_layout(dw.trie)):
+        ci = child_index(dw.trie, depth)
+        masks = child_index_masks(dw.trie, depth).cpu().numpy().view(np.uint32)
+        for node in range(d.node_lo, d.node_hi, max(1, (d.node_hi - d.node_lo) // 97)):
+            s0 = rp[node]
+            e0 = rp[node + 1] if node + 1 < rp.size else nnz
+            want = np.zeros(8, np.uint32)
+            for t in cv[0, s0:e0] - ci.window_lo:
+                want[t >> 5] |= np.uint32(1) << np.uint32(t & 31)
+            np.testing.assert_array_equal(masks[node - d.node_lo], want)
