@@ -43,16 +43,22 @@ class DepthLayout(NamedTuple):
     window_n: int
 
 
-_LAYOUT_CACHE: "weakref.WeakKeyDictionary" = weakref.WeakKeyDictionary()
+_LAYOUT_CACHE: dict = {}  # id(row_ptrs) -> (weakref to row_ptrs, {version key: slot})
 
 
 def _cache_slot(trie: CompactCSRTrie) -> dict:
-    """Per-trie cache, held weakly by the trie's row_ptrs tensor and keyed by
-    both arrays' identity and version counters (an in-place edit or a new
-    array invalidates it; the cached entry keeps the arrays it was built
-    from alive, so their memory cannot be reused under it)."""
-    per = _LAYOUT_CACHE.setdefault(trie.row_ptrs, {})
-    key = (id(trie.stacked_cols_vals), trie.stacked_cols_vals._version, trie.row_ptrs._version)
+    """Per-trie cache, dropped when the trie's row_ptrs tensor is freed and
+    keyed by both arrays' identity and version counters (an in-place edit or
+    a new array invalidates it; the entry keeps the arrays it was built from
+    alive, so their memory cannot be reused under it)."""
+    rp = trie.row_ptrs
+    ent = _LAYOUT_CACHE.get(id(rp))
+    if ent is None or ent[0]() is not rp:
+        ent = (weakref.ref(rp), {})
+        _LAYOUT_CACHE[id(rp)] = ent
+        weakref.finalize(rp, _LAYOUT_CACHE.pop, id(rp), None)
+    per = ent[1]
+    key = (id(trie.stacked_cols_vals), trie.stacked_cols_vals._version, rp._version)
     slot = per.get(key)
     if slot is None:
         per.clear()

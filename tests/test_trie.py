@@ -88,3 +88,21 @@ def test_level_windows_cover_children():
     assert wins == [(l * 256, 256) if l < 3 else wins[3] for l in range(4)]
     lo, n = wins[3]
     assert 768 <= lo and lo + n <= 1024
+
+
+def test_depth_layout_cache_follows_the_trie():
+    import gc
+
+    from rectokens_b200.decoding import beam_search as B
+
+    w = S.WORKLOADS["cfg1"]
+    tok = torch.from_numpy(S.to_tokens(w.make_catalog(), w.codes))
+    csr = CompactCSRTrie.from_sorted_batch(tok, vocab_size=w.vocab, dense_lookup_layers=1)
+    first = B.depth_layout(csr)
+    assert B.depth_layout(csr) is first                     # cached
+    csr.stacked_cols_vals[0, 0] += 0                         # in-place edit bumps the version
+    assert B.depth_layout(csr) is not first
+    n = len(B._LAYOUT_CACHE)
+    del csr
+    gc.collect()
+    assert len(B._LAYOUT_CACHE) == n - 1                     # dropped with the trie
