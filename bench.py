@@ -416,7 +416,7 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16" if w.dtype == "bf16" else "f32",
                 "data": "synthetic (seeded catalog, N(0,0.02) head, N(0,1) hidden states)",
                 "config": workload_cfg, "clocks": clk, "roofline": roof,
