@@ -187,6 +187,25 @@ size_t vtnk_beam_search_workspace_bytes(const vtnk_search_t* s);
 int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_bytes,
                      int64_t* out_ids, float* out_logp, int64_t* out_node, void* stream);
 
+/* Size of the scratch array built into the library for
+ * vtnk_beam_search_noalloc (held on every GPU that loads the library). */
+#define VTNK_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* vtnk_beam_search without a caller workspace, for callers that may not
+ * allocate device memory on the decode path (a plugin whose host process owns
+ * all device memory through its own pool, or code that must avoid the device
+ * synchronisation an allocation can trigger).  Inputs and outputs are as for
+ * vtnk_beam_search; the scratch is a fixed array of VTNK_NOALLOC_SCRATCH_BYTES
+ * inside the library, so searches whose vtnk_beam_search_workspace_bytes
+ * exceed it are rejected (VTNK_ERR_UNSUPPORTED, message names both sizes).
+ * The first call on each device looks up that array's device address (make
+ * it with the device current, before any stream capture).  Every call on a
+ * device shares the one array: calls that overlap on the GPU (different
+ * streams, or host threads) race and corrupt each other's results.  No
+ * counterpart in the reference. */
+int vtnk_beam_search_noalloc(const vtnk_search_t* s, int64_t* out_ids, float* out_logp,
+                             int64_t* out_node, void* stream);
+
 /* Synthetic hidden states (benchmark / test input generator, no reference
  * counterpart): out[r, h] = table[mix64(key(seed, stream_id) ^ ((row0 + r) * H + h)) >> 48]
  * with the 65,536-entry quantile table given as bf16 bits (dtype BF16) or fp32

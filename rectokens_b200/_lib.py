@@ -28,6 +28,7 @@ EXPORTS = (
     "vtnk_beam_merge",
     "vtnk_beam_search_workspace_bytes",
     "vtnk_beam_search",
+    "vtnk_beam_search_noalloc",
     "vtnk_synth_normal",
     "vtnk_device_status",
     "vtnk_last_error",
@@ -87,6 +88,7 @@ def lib() -> ctypes.CDLL:
                                P, P, P, P, V],
             "vtnk_beam_merge": [I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, V],
             "vtnk_beam_search": [POINTER(Search), P, c_size_t, P, P, P, V],
+            "vtnk_beam_search_noalloc": [POINTER(Search), P, P, P, V],
             "vtnk_synth_normal": [c_uint64, c_uint64, I64, I64, I64, P, c_int32, P, V],
         }
         for name, args in sig.items():
