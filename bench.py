@@ -67,7 +67,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100", "-i", str(self.gpu)],
+                 "-lms", "20", "-i", str(self.gpu)],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
@@ -186,9 +186,11 @@ class CpuBaseline:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--workload", default="cfg5")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the workload's query count (smaller cases for profiling)")
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--cpu-queries", type=int, default=0,
@@ -203,6 +205,10 @@ def main():
     from rectokens_b200 import synthetic as S
 
     w = S.WORKLOADS[args.workload]
+    if args.batch:
+        import dataclasses
+
+        w = dataclasses.replace(w, batch=args.batch)
     workload_cfg = {
         "workload": f"{args.workload}: {w.levels}-level beam search, catalog K={w.codes} "
                     f"L={w.levels}, H={w.hidden} {w.dtype} head, batch {w.batch} x {w.beams} "

@@ -52,7 +52,8 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
 
     def compile_one(so):
         s, o = so
-        cmd = [cc, *ARCH, *FLAGS, *(extra or []), "-c", str(s), "-o", str(o)]
+        env_extra = os.environ.get("VTNK_NVCC_EXTRA", "").split()
+        cmd = [cc, *ARCH, *FLAGS, *(extra or []), *env_extra, "-c", str(s), "-o", str(o)]
         if verbose:
             print(" ".join(cmd), flush=True)
         r = subprocess.run(cmd, capture_output=True, text=True)

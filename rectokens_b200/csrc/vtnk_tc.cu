@@ -38,7 +38,10 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
+#ifndef VTNK_TC_STAGES
+#define VTNK_TC_STAGES 4
+#endif
+constexpr int STAGES = VTNK_TC_STAGES;
 constexpr int A_BYTES = BM * BK * 2;
 constexpr int B_BYTES = BN * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -130,6 +133,37 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatil
     }
   }
 }
+// Warp-level wait for the epilogue: one lane polls, with a growing sleep
+// between polls, so 128 waiting threads do not compete with the tensor
+// core's operand reads for shared memory.  Result in every lane.
+__device__ __forceinline__ bool warp_wait_phase(uint64_t* b, uint32_t parity, volatile int* abort,
+                                                int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    if (!mbar_try_wait(b, parity)) {
+      const uint64_t t0 = gtimer();
+      uint32_t ns = 32;
+      for (;;) {
+        __nanosleep(ns);
+        if (mbar_try_wait(b, parity)) break;
+        if (ns < 512) ns <<= 1;
+        if (*abort) {
+          ok = 0;
+          break;
+        }
+        if (gtimer() - t0 > WAIT_LIMIT_NS) {
+          *abort = 1;
+          atomicCAS(&g_tc_status, 0, code);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  return ok != 0;
+}
+
 // Drain wait at teardown: bounded, never sets abort.
 __device__ __forceinline__ void drain_phase(uint64_t* b, uint32_t parity) {
   const uint64_t t0 = gtimer();
@@ -210,19 +244,21 @@ struct TopN {
   }
   // Larger value first; an equal value never displaces an earlier entry, so
   // feeding columns in increasing order breaks ties toward the lower column.
+  // The insert position is a count of entries >= x and every slot is then
+  // updated by an independent select from the old values: short dependency
+  // chains, so one warp per scheduler keeps issuing.
   __device__ __forceinline__ void push(float x, int col) {
     if (!(x > v[NC - 1])) return;
+    int pos = 0;
 #pragma unroll
-    for (int i = 0; i < NC; ++i) {
-      if (x > v[i]) {
-        const float tv = v[i];
-        const int tc = c[i];
-        v[i] = x;
-        c[i] = col;
-        x = tv;
-        col = tc;
-      }
+    for (int i = 0; i < NC; ++i) pos += (v[i] >= x) ? 1 : 0;
+#pragma unroll
+    for (int i = NC - 1; i > 0; --i) {
+      v[i] = (i > pos) ? v[i - 1] : ((i == pos) ? x : v[i]);
+      c[i] = (i > pos) ? c[i - 1] : ((i == pos) ? col : c[i]);
     }
+    v[0] = (pos == 0) ? x : v[0];
+    c[0] = (pos == 0) ? col : c[0];
   }
 };
 
@@ -301,7 +337,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
-      uint32_t armed[STAGES] = {0, 0, 0, 0};
+      uint32_t armed[STAGES] = {};
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -395,9 +431,10 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
 
       const uint32_t buf = it & 1;
-      const bool ok = wait_phase(&S.tfull[buf], (it >> 1) & 1, abort, 4);
-      __syncwarp();
-      if (__any_sync(0xffffffffu, !ok)) break;
+      const bool ok = warp_wait_phase(&S.tfull[buf], (it >> 1) & 1, abort, 4);
+      if (!ok) break;
+      // every lane observes the completed phase before touching TMEM
+      mbar_try_wait(&S.tfull[buf], (it >> 1) & 1);
       tc_fence_after();
 
       TopN<NC> top;
@@ -635,6 +672,13 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
       !make_map(&mw, t.w, t.H, t.n_vocab, t.w_stride * 2, BK, BN)) {
     set_error("cuTensorMapEncodeTiled failed");
     return VTNK_ERR_CUDA;
+  }
+  switch (t.n_cand) {  // exact widths for the common beam sizes
+    case 1: return launch_nc<1>(ma, mw, p, s);
+    case 5: return launch_nc<5>(ma, mw, p, s);
+    case 10: return launch_nc<10>(ma, mw, p, s);
+    case 20: return launch_nc<20>(ma, mw, p, s);
+    default: break;
   }
   if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, s);
   if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, s);
