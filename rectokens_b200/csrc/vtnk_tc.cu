@@ -33,6 +33,18 @@ namespace vtnk {
 
 __device__ int g_tc_status = 0;  // 0 ok; else the first failing wait's code
 
+// Phase timers for tuning builds (-DVTNK_TC_PROFILE): cycles summed over CTAs.
+#ifdef VTNK_TC_PROFILE
+__device__ unsigned long long g_prof[8];
+#define PROF_T0(name) const long long name = clock64()
+#define PROF_ACC(acc, t0) acc += clock64() - (t0)
+#define PROF_FLUSH(i, acc) atomicAdd(&g_prof[i], static_cast<unsigned long long>(acc))
+#else
+#define PROF_T0(name)
+#define PROF_ACC(acc, t0)
+#define PROF_FLUSH(i, acc)
+#endif
+
 namespace tc {
 
 constexpr int BM = 128;
@@ -52,6 +64,7 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
 
 struct Shared {
   uint8_t ring[STAGES][STAGE_BYTES];  // 1024-aligned stages
+  float chunk_x[EPI_WARPS][32][32];    // epilogue: one 32-column chunk per warp, [col][lane]
   float bias[BN];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -121,9 +134,12 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatil
                                            int code) {
   if (mbar_try_wait(b, parity)) return true;
   const uint64_t t0 = gtimer();
+  uint32_t ns = 0;
   for (uint32_t i = 1;; ++i) {
+    if (ns) __nanosleep(ns);  // back off so a waiting role does not steal issue slots
     if (mbar_try_wait(b, parity)) return true;
-    if ((i & 31) == 0) {
+    if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
+    if ((i & 15) == 0) {
       if (*abort) return false;
       if (gtimer() - t0 > WAIT_LIMIT_NS || i > (1u << 30)) {
         *abort = 1;
@@ -249,6 +265,11 @@ struct TopN {
   // chains, so one warp per scheduler keeps issuing.
   __device__ __forceinline__ void push(float x, int col) {
     if (!(x > v[NC - 1])) return;
+    insert(x, col);
+  }
+  // Branch-free insert: a value not above the current n-th largest gets
+  // pos == NC and leaves the list unchanged.
+  __device__ __forceinline__ void insert(float x, int col) {
     int pos = 0;
 #pragma unroll
     for (int i = 0; i < NC; ++i) pos += (v[i] >= x) ? 1 : 0;
@@ -261,6 +282,18 @@ struct TopN {
     c[0] = (pos == 0) ? col : c[0];
   }
 };
+
+template <int N>
+__device__ __forceinline__ float tree_max(const float (&x)[N]) {
+  float t[N / 2];
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) t[i] = fmaxf(x[2 * i], x[2 * i + 1]);
+#pragma unroll
+  for (int w = N / 4; w >= 1; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) t[i] = fmaxf(t[2 * i], t[2 * i + 1]);
+  return t[0];
+}
 
 // Exact per-row path for a row whose node is outside the index or whose
 // children are not a clean sorted in-window set (slow, never taken for a
@@ -338,15 +371,18 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
       uint32_t armed[STAGES] = {};
+      long long prof_wait = 0;
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
       for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
         for (int kb = 0; kb < kblocks; ++kb) {
+          PROF_T0(t_w);
           if (!wait_phase(&S.empty[stage], phase ^ 1, abort, 1)) {
             ok = false;
             break;
           }
+          PROF_ACC(prof_wait, t_w);
           uint8_t* st = S.ring[stage];
           mbar_expect_tx(&S.full[stage], STAGE_BYTES);
           tma_load_2d(st, &tmA, &S.full[stage], kb * BK, static_cast<int>(tile * BM));
@@ -361,6 +397,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // copies still in flight land before the CTA exits
       for (int s = 0; s < STAGES; ++s)
         if (armed[s]) drain_phase(&S.full[s], (armed[s] - 1) & 1);
+      PROF_FLUSH(0, prof_wait);
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
@@ -369,16 +406,21 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       uint32_t phase = 0;
       uint32_t it = 0;
       bool ok = true;
+      long long prof_full = 0, prof_tempty = 0;
       for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
         const uint32_t buf = it & 1;
+        PROF_T0(t_e);
         if (!wait_phase(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)) break;
+        PROF_ACC(prof_tempty, t_e);
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
         for (int kb = 0; kb < kblocks; ++kb) {
+          PROF_T0(t_f);
           if (!wait_phase(&S.full[stage], phase, abort, 3)) {
             ok = false;
             break;
           }
+          PROF_ACC(prof_full, t_f);
           tc_fence_after();
           const uint64_t da = umma_desc_sw128(S.ring[stage]);
           const uint64_t db = umma_desc_sw128(S.ring[stage] + A_BYTES);
@@ -395,13 +437,17 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
       umma_commit(&S.mma_done);
       drain_phase(&S.mma_done, 0);
+      PROF_FLUSH(1, prof_full);
+      PROF_FLUSH(2, prof_tempty);
     }
   } else {
     // ---------------------------------------------------------------- epilogue
     const int lg = warp & 3;             // TMEM lane group this warp may access
     const int r_local = lg * 32 + lane;  // row within the tile == TMEM lane
     uint32_t it = 0;
+    long long pe_pro = 0, pe_wait = 0, pe_tmem = 0, pe_out = 0, pe_ld = 0;
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+      PROF_T0(t_pro);
       const int64_t row = tile * BM + r_local;
       const bool live = row < p.rows;
       // The row's children as a 256-bit mask over the window, read from the
@@ -430,49 +476,83 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         spill = pc != count;
       }
 
+      PROF_ACC(pe_pro, t_pro);
+      PROF_T0(t_wt);
       const uint32_t buf = it & 1;
       const bool ok = warp_wait_phase(&S.tfull[buf], (it >> 1) & 1, abort, 4);
       if (!ok) break;
       // every lane observes the completed phase before touching TMEM
       mbar_try_wait(&S.tfull[buf], (it >> 1) & 1);
       tc_fence_after();
+      PROF_ACC(pe_wait, t_wt);
+      PROF_T0(t_tm);
 
       TopN<NC> top;
       top.init();
       float mx = -INFINITY, sum = 0.f;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BN;
+      const bool has_bias = p.bias != nullptr;
 #pragma unroll 1
       for (int chunk = 0; chunk < BN / 32; ++chunk) {
         uint32_t v[32];
         __syncwarp();
+        PROF_T0(t_ld);
         tmem_ld32(taddr + chunk * 32, v);  // warp-collective: every lane, every chunk
+        PROF_ACC(pe_ld, t_ld);
         uint32_t mw = 0;
 #pragma unroll
         for (int i = 0; i < BN / 32; ++i) mw = (i == chunk) ? m[i] : mw;
-        float cm = -INFINITY;
+        float x[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float x = __uint_as_float(v[i]) + S.bias[chunk * 32 + i];
-          v[i] = __float_as_uint(x);
-          if ((mw >> i) & 1u) cm = fmaxf(cm, x);
+          float y = __uint_as_float(v[i]);
+          if (has_bias) y += S.bias[chunk * 32 + i];
+          x[i] = ((mw >> i) & 1u) ? y : -INFINITY;
         }
-        if (cm > mx) {
-          sum *= __expf(mx - cm);
-          mx = cm;
-        }
+        // online log-sum-exp over the chunk's children
+        const float nm = fmaxf(mx, tree_max<32>(x));
+        sum *= (nm == mx) ? 1.f : __expf(mx - nm);
+        mx = nm;
+        float e[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) e[i] = (x[i] > -INFINITY) ? __expf(x[i] - mx) : 0.f;
+#pragma unroll
+        for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+          for (int i = 0; i < w; ++i) e[i] += e[i + w];
+        sum += e[0];
+        // top-n: each lane inserts only its values above its current n-th best,
+        // in column order (ties keep the lower column); the warp loops
+        // max-over-lanes(candidates) times.  Values are read back from shared
+        // memory ([col][lane]: conflict-free for any per-lane column).
+        const float thr = top.v[NC - 1];
+        uint32_t pend = 0;
+        float* sx = &S.chunk_x[warp - 2][0][0];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          if ((mw >> i) & 1u) {
-            const float x = __uint_as_float(v[i]);
-            sum += __expf(x - mx);
-            top.push(x, chunk * 32 + i);
+          pend |= (x[i] > thr) ? (1u << i) : 0u;
+          sx[i * 32 + lane] = x[i];
+        }
+        __syncwarp();
+        while (__any_sync(0xffffffffu, pend != 0u)) {
+          float y = -INFINITY;
+          int col = 0;
+          if (pend) {
+            const int i = __ffs(pend) - 1;
+            pend &= pend - 1;
+            y = sx[i * 32 + lane];
+            col = chunk * 32 + i;
           }
+          top.insert(y, col);  // no-op for -inf / values no longer above the n-th best
         }
+        __syncwarp();
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.tempty[buf]);
 
+      PROF_ACC(pe_tmem, t_tm);
+      PROF_T0(t_out);
       float lse = (mx > -INFINITY) ? mx + __logf(sum) : -INFINITY;
       bool by_slot = false;
       if (spill && live) {  // exact scalar recompute of this row
@@ -523,6 +603,14 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         p.row_lse[row] = lse;
       }
+      PROF_ACC(pe_out, t_out);
+    }
+    if (lane == 0) {
+      PROF_FLUSH(3, pe_pro);
+      PROF_FLUSH(4, pe_wait);
+      PROF_FLUSH(5, pe_tmem);
+      PROF_FLUSH(6, pe_out);
+      PROF_FLUSH(7, pe_ld);
     }
   }
 
@@ -711,3 +799,16 @@ int read_tc_status(int* out, bool reset) {
 }
 
 }  // namespace vtnk
+
+#ifdef VTNK_TC_PROFILE
+// Tuning builds only: copy (and optionally clear) the phase timers.
+extern "C" int vtnk_tc_profile(unsigned long long* out, int reset) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, vtnk::g_prof, sizeof(unsigned long long) * 8);
+  if (reset) {
+    unsigned long long z[8] = {};
+    cudaMemcpyToSymbol(vtnk::g_prof, z, sizeof(z));
+  }
+  return 0;
+}
+#endif
