@@ -8,13 +8,16 @@
 // that are not children of a row's node are dropped in the epilogue, using
 // the depth's child-bitmask index (32 bytes per node, built once per trie).
 //
-// CTA layout (persistent, one CTA per SM, 192 threads):
+// CTA layout (persistent, one CTA per SM, 320 threads):
 //   warp 0      TMA producer      A tile [128 x 64] + W tile [256 x 64] per stage
 //   warp 1      MMA issuer        tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16
 //                                 (also allocates / frees 512 TMEM columns)
-//   warps 2..5  epilogue          thread = row: tcgen05.ld 32x32b, mask, top-n, LSE
-// Shared memory: 4 stages x 48 KB operand ring (SWIZZLE_128B, K-major), the
-// window's bias, mbarriers.  TMEM holds two 128 x 256 fp32 accumulators so
+//   warps 2..9  epilogue          thread = row: tcgen05.ld 32x32b, mask, top-n, LSE;
+//                                 two warps per TMEM lane group split the 256
+//                                 columns, the upper half hands its partial
+//                                 result to the lower half
+// Shared memory: 3 stages x 48 KB operand ring (SWIZZLE_128B, K-major), the
+// epilogue's chunk staging and hand-off buffers, the window's bias, mbarriers.  TMEM holds two 128 x 256 fp32 accumulators so
 // the epilogue of tile i overlaps the MMAs of tile i + 1.
 //
 // Every mbarrier wait is bounded in time; on expiry the CTA records a status
@@ -50,14 +53,16 @@ namespace tc {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;
+constexpr int PAIR_M = 2 * BM;  // rows per CTA pair (one cta_group::2 MMA tile)
 #ifndef VTNK_TC_STAGES
 #define VTNK_TC_STAGES 4
 #endif
 constexpr int STAGES = VTNK_TC_STAGES;
-constexpr int A_BYTES = BM * BK * 2;
-constexpr int B_BYTES = BN * BK * 2;
+constexpr int A_BYTES = BM * BK * 2;        // this CTA's 128 rows
+constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's half of the 256 window rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane group, splitting the 256 columns
+constexpr int MAX_NC = 32;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
@@ -65,11 +70,14 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
 struct Shared {
   uint8_t ring[STAGES][STAGE_BYTES];  // 1024-aligned stages
   float chunk_x[EPI_WARPS][32][32];    // epilogue: one 32-column chunk per warp, [col][lane]
+  float merge[4][2 * MAX_NC + 2][32];  // upper-half warp -> lower-half warp partial results
   float bias[BN];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
+  uint64_t merge_full[4];
+  uint64_t merge_empty[4];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
@@ -149,6 +157,68 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatil
     }
   }
 }
+// --- CTA-pair helpers (cluster of two CTAs sharing one cta_group::2 MMA)
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t map_to_rank(const void* p, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(su32(p)), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                   : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (for arrivals from the peer CTA).
+__device__ __forceinline__ bool wait_phase_cluster(uint64_t* b, uint32_t parity,
+                                                   volatile int* abort, int code) {
+  if (mbar_try_wait_cluster(b, parity)) return true;
+  const uint64_t t0 = gtimer();
+  uint32_t ns = 0;
+  for (uint32_t i = 1;; ++i) {
+    if (ns) __nanosleep(ns);
+    if (mbar_try_wait_cluster(b, parity)) return true;
+    if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
+    if ((i & 15) == 0) {
+      if (*abort) return false;
+      if (gtimer() - t0 > WAIT_LIMIT_NS || i > (1u << 30)) {
+        *abort = 1;
+        atomicCAS(&g_tc_status, 0, code);
+        return false;
+      }
+    }
+  }
+}
+// TMA load into this CTA's shared memory whose completion is counted on the
+// pair leader's barrier (cluster address); no multicast.
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map,
+                                                 uint32_t leader_bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
+      : "memory");
+}
+
 // Warp-level wait for the epilogue: one lane polls, with a growing sleep
 // between polls, so 128 waiting threads do not compete with the tensor
 // core's operand reads for shared memory.  Result in every lane.
@@ -207,23 +277,26 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem) {
          | (2ull << 61);                              // layout: SWIZZLE_128B
 }
 // Instruction descriptor: kind::f16, A = B = bf16, D = fp32, both K-major,
-// N = 256, M = 128.
+// N = 256, M = 256 (a cta_group::2 pair, 128 rows per CTA).
 constexpr uint32_t IDESC =
-    (1u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((BM >> 4) << 24);
+    (1u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((PAIR_M >> 4) << 24);
 
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t da, uint64_t db,
                                           uint32_t accumulate) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(da), "l"(db), "r"(IDESC), "r"(accumulate)
       : "memory");
 }
-__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+// Arrive on barrier `bar` (same offset) in both CTAs of the pair once all
+// previously issued MMAs of this thread are complete.
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
   asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-          su32(bar))
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], m;\n\t}" ::"r"(su32(bar))
       : "memory");
 }
 __device__ __forceinline__ void tc_fence_before() {
@@ -323,7 +396,7 @@ __device__ void row_scalar(const Params& p, int64_t row, int64_t start, int coun
 }
 
 template <int NC>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                  const Params p) {
   extern __shared__ uint8_t smem_raw[];
@@ -331,29 +404,36 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                                          ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int64_t n_tiles = (p.rows + BM - 1) / BM;
+  const uint32_t rank = cluster_rank();            // 0 = pair leader (issues the MMAs)
+  const int64_t pair = blockIdx.x >> 1;
+  const int64_t n_pairs = gridDim.x >> 1;
+  const int64_t n_tiles = (p.rows + PAIR_M - 1) / PAIR_M;  // 256-row tiles, one per pair step
   const int kblocks = static_cast<int>((p.H + BK - 1) / BK);
   volatile int* abort = &S.abort;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&S.full[s], 1);
-      mbar_init(&S.empty[s], 1);
+      mbar_init(&S.full[s], 1);   // leader: its expect_tx arrival + both CTAs' bytes
+      mbar_init(&S.empty[s], 1);  // both: the leader's MMA commit
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&S.tfull[b], 1);
-      mbar_init(&S.tempty[b], EPI_WARPS);
+      mbar_init(&S.tfull[b], 1);                // both: the leader's MMA commit
+      mbar_init(&S.tempty[b], 2 * EPI_WARPS);   // leader: every epilogue warp of the pair
+    }
+    for (int g = 0; g < 4; ++g) {
+      mbar_init(&S.merge_full[g], 32);
+      mbar_init(&S.merge_empty[g], 32);
     }
     mbar_init(&S.mma_done, 1);
     S.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+  if (warp == 1) {  // same warp and same smem offset in both CTAs
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                      su32(&S.tmem_base)),
                  "r"(TMEM_COLS)
                  : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   for (int i = threadIdx.x; i < BN; i += THREADS) {
     const int64_t col = p.window_lo + i;
@@ -362,11 +442,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
 
   if (warp == 0) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- TMA producer (both CTAs)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
@@ -375,7 +456,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x) {
+      const int wrow = static_cast<int>(p.window_lo) + static_cast<int>(rank) * (BN / 2);
+      for (int64_t tile = pair; ok && tile < n_tiles; tile += n_pairs) {
+        const int arow = static_cast<int>(tile * PAIR_M) + static_cast<int>(rank) * BM;
         for (int kb = 0; kb < kblocks; ++kb) {
           PROF_T0(t_w);
           if (!wait_phase(&S.empty[stage], phase ^ 1, abort, 1)) {
@@ -384,9 +467,10 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
           PROF_ACC(prof_wait, t_w);
           uint8_t* st = S.ring[stage];
-          mbar_expect_tx(&S.full[stage], STAGE_BYTES);
-          tma_load_2d(st, &tmA, &S.full[stage], kb * BK, static_cast<int>(tile * BM));
-          tma_load_2d(st + A_BYTES, &tmW, &S.full[stage], kb * BK, static_cast<int>(p.window_lo));
+          if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * STAGE_BYTES);
+          const uint32_t lbar = map_to_rank(&S.full[stage], 0);
+          tma_load_2d_pair(st, &tmA, lbar, kb * BK, arow);
+          tma_load_2d_pair(st + A_BYTES, &tmW, lbar, kb * BK, wrow);
           ++armed[stage];
           if (++stage == STAGES) {
             stage = 0;
@@ -394,23 +478,25 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
         }
       }
-      // copies still in flight land before the CTA exits
-      for (int s = 0; s < STAGES; ++s)
-        if (armed[s]) drain_phase(&S.full[s], (armed[s] - 1) & 1);
+      // the leader's barriers count both CTAs' copies: it waits for any still in
+      // flight; the peer stays resident until the teardown cluster barrier
+      if (rank == 0)
+        for (int s = 0; s < STAGES; ++s)
+          if (armed[s]) drain_phase(&S.full[s], (armed[s] - 1) & 1);
       PROF_FLUSH(0, prof_wait);
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // ---------------------------------------------------------------- MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t it = 0;
       bool ok = true;
       long long prof_full = 0, prof_tempty = 0;
-      for (int64_t tile = blockIdx.x; ok && tile < n_tiles; tile += gridDim.x, ++it) {
+      for (int64_t tile = pair; ok && tile < n_tiles; tile += n_pairs, ++it) {
         const uint32_t buf = it & 1;
         PROF_T0(t_e);
-        if (!wait_phase(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)) break;
+        if (!wait_phase_cluster(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)) break;
         PROF_ACC(prof_tempty, t_e);
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
@@ -427,15 +513,15 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)  // +32 B per K=16 step inside the swizzle atom
             umma_bf16(d, da + 2 * k, db + 2 * k, (kb | k) != 0);
-          umma_commit(&S.empty[stage]);
+          umma_commit_pair(&S.empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        if (ok) umma_commit(&S.tfull[buf]);
+        if (ok) umma_commit_pair(&S.tfull[buf]);
       }
-      umma_commit(&S.mma_done);
+      umma_commit_pair(&S.mma_done);
       drain_phase(&S.mma_done, 0);
       PROF_FLUSH(1, prof_full);
       PROF_FLUSH(2, prof_tempty);
@@ -443,12 +529,14 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   } else {
     // ---------------------------------------------------------------- epilogue
     const int lg = warp & 3;             // TMEM lane group this warp may access
+    const int half = (warp - 2) >> 2;    // 0: columns 0..127 (+ merge, outputs); 1: 128..255
     const int r_local = lg * 32 + lane;  // row within the tile == TMEM lane
     uint32_t it = 0;
     long long pe_pro = 0, pe_wait = 0, pe_tmem = 0, pe_out = 0, pe_ld = 0;
-    for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++it) {
+    const uint32_t tempty_leader[2] = {map_to_rank(&S.tempty[0], 0), map_to_rank(&S.tempty[1], 0)};
+    for (int64_t tile = pair; tile < n_tiles; tile += n_pairs, ++it) {
       PROF_T0(t_pro);
-      const int64_t row = tile * BM + r_local;
+      const int64_t row = tile * PAIR_M + static_cast<int64_t>(rank) * BM + r_local;
       const bool live = row < p.rows;
       // The row's children as a 256-bit mask over the window, read from the
       // depth's child index (two 16-byte loads).  A row whose node is outside
@@ -493,7 +581,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BN;
       const bool has_bias = p.bias != nullptr;
 #pragma unroll 1
-      for (int chunk = 0; chunk < BN / 32; ++chunk) {
+      for (int chunk = half * (BN / 64); chunk < (half + 1) * (BN / 64); ++chunk) {
         uint32_t v[32];
         __syncwarp();
         PROF_T0(t_ld);
@@ -549,7 +637,44 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&S.tempty[buf]);
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);  // the leader's MMA may reuse it
+
+      // The upper-half warp hands (top-n, max, sum) to the lower-half warp of
+      // the same rows through shared memory; bounded waits on both sides.
+      float (*mg)[32] = S.merge[lg];
+      if (half == 1) {
+        if (!warp_wait_phase(&S.merge_empty[lg], (it & 1) ^ 1, abort, 5)) break;
+        mbar_try_wait(&S.merge_empty[lg], (it & 1) ^ 1);
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+          mg[j][lane] = top.v[j];
+          mg[MAX_NC + j][lane] = __int_as_float(top.c[j]);
+        }
+        mg[2 * MAX_NC][lane] = mx;
+        mg[2 * MAX_NC + 1][lane] = sum;
+        mbar_arrive(&S.merge_full[lg]);
+        PROF_ACC(pe_tmem, t_tm);
+        continue;
+      }
+      if (!warp_wait_phase(&S.merge_full[lg], it & 1, abort, 6)) break;
+      mbar_try_wait(&S.merge_full[lg], it & 1);
+      {
+        const float omx = mg[2 * MAX_NC][lane];
+        const float osum = mg[2 * MAX_NC + 1][lane];
+        const float nm = fmaxf(mx, omx);
+        sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) +
+              (omx > -INFINITY ? osum * __expf(omx - nm) : 0.f);
+        mx = nm;
+        // the other half's columns are all higher: inserting its sorted list
+        // after ours keeps ties on the lower column
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+          const float y = mg[j][lane];
+          const int c = __float_as_int(mg[MAX_NC + j][lane]);
+          if (__any_sync(0xffffffffu, y > top.v[NC - 1])) top.insert(y, c);
+        }
+      }
+      mbar_arrive(&S.merge_empty[lg]);
 
       PROF_ACC(pe_tmem, t_tm);
       PROF_T0(t_out);
@@ -617,9 +742,10 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   // ------------------------------------------------------------------ teardown
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // the pair's MMAs and copies are done before either CTA frees or exits
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
                  "r"(TMEM_COLS)
                  : "memory");
   }
@@ -707,9 +833,9 @@ int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, cudaS
   auto k = beam_step_kernel<NC>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(SMEM_BYTES));
-  const int64_t tiles = (p.rows + BM - 1) / BM;
-  const int sms = sm_count();
-  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  const int64_t pairs = (p.rows + PAIR_M - 1) / PAIR_M;  // one 256-row tile per pair step
+  const int max_pairs = sm_count() / 2;
+  const int grid = 2 * static_cast<int>(pairs < max_pairs ? pairs : max_pairs);
   k<<<grid, THREADS, SMEM_BYTES, s>>>(a, w, p);
   return cuda_status(cudaGetLastError(), "beam_step_tc launch");
 }
@@ -729,6 +855,7 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   using namespace tc;
   auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
   if (!t.masks || !aligned(t.masks) || t.idx_hi < t.idx_lo || t.window_n < 1 ||
+      t.window_lo + BN > (int64_t(1) << 31) ||
       t.window_n > BN || t.n_cand < 1 || t.n_cand > 32 || t.rows < 1 || t.H % 8 != 0 ||
       t.a_stride % 8 != 0 || t.w_stride % 8 != 0 || !aligned(t.a) || !aligned(t.w) || t.mb < 1 ||
       t.window_lo < 0 || t.rows > (int64_t(1) << 31) - BM)
@@ -757,7 +884,7 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.row_lse = t.row_lse;
   CUtensorMap ma, mw;
   if (!make_map(&ma, t.a, t.H, t.rows, t.a_stride * 2, BK, BM) ||
-      !make_map(&mw, t.w, t.H, t.n_vocab, t.w_stride * 2, BK, BN)) {
+      !make_map(&mw, t.w, t.H, t.n_vocab, t.w_stride * 2, BK, BN / 2)) {
     set_error("cuTensorMapEncodeTiled failed");
     return VTNK_ERR_CUDA;
   }
