@@ -55,7 +55,7 @@ constexpr int BN = 256;
 constexpr int BK = 64;
 constexpr int PAIR_M = 2 * BM;  // rows per CTA pair (one cta_group::2 MMA tile)
 #ifndef VTNK_TC_STAGES
-#define VTNK_TC_STAGES 4
+#define VTNK_TC_STAGES 5
 #endif
 constexpr int STAGES = VTNK_TC_STAGES;
 constexpr int A_BYTES = BM * BK * 2;        // this CTA's 128 rows
@@ -70,7 +70,8 @@ constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
 struct Shared {
   uint8_t ring[STAGES][STAGE_BYTES];  // 1024-aligned stages
   float chunk_x[EPI_WARPS][32][32];    // epilogue: one 32-column chunk per warp, [col][lane]
-  float merge[4][2 * MAX_NC + 2][32];  // upper-half warp -> lower-half warp partial results
+  float merge[4][MAX_NC + MAX_NC / 4 + 2][32];  // upper-half -> lower-half partial results:
+                                                // NC values, NC byte-packed columns, max, sum
   float bias[BN];
   uint64_t full[STAGES];
   uint64_t empty[STAGES];
@@ -622,6 +623,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           sx[i * 32 + lane] = x[i];
         }
         __syncwarp();
+#ifdef VTNK_TC_EXPERIMENT_NOSELECT
+        pend = 0u;  // tuning experiment only: measures the pipeline without top-n work
+#endif
         while (__any_sync(0xffffffffu, pend != 0u)) {
           float y = -INFINITY;
           int col = 0;
@@ -646,12 +650,18 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (!warp_wait_phase(&S.merge_empty[lg], (it & 1) ^ 1, abort, 5)) break;
         mbar_try_wait(&S.merge_empty[lg], (it & 1) ^ 1);
 #pragma unroll
-        for (int j = 0; j < NC; ++j) {
-          mg[j][lane] = top.v[j];
-          mg[MAX_NC + j][lane] = __int_as_float(top.c[j]);
+        for (int j = 0; j < NC; ++j) mg[j][lane] = top.v[j];
+#pragma unroll
+        for (int j = 0; j < NC; j += 4) {  // columns < 256: four per word, 0xFF = none
+          uint32_t w = 0;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (j + q < NC) w |= static_cast<uint32_t>(top.c[j + q] & 0xFF) << (8 * q);
+            else w |= 0xFFu << (8 * q);
+          mg[MAX_NC + j / 4][lane] = __uint_as_float(w);
         }
-        mg[2 * MAX_NC][lane] = mx;
-        mg[2 * MAX_NC + 1][lane] = sum;
+        mg[MAX_NC + MAX_NC / 4][lane] = mx;
+        mg[MAX_NC + MAX_NC / 4 + 1][lane] = sum;
         mbar_arrive(&S.merge_full[lg]);
         PROF_ACC(pe_tmem, t_tm);
         continue;
@@ -659,8 +669,8 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       if (!warp_wait_phase(&S.merge_full[lg], it & 1, abort, 6)) break;
       mbar_try_wait(&S.merge_full[lg], it & 1);
       {
-        const float omx = mg[2 * MAX_NC][lane];
-        const float osum = mg[2 * MAX_NC + 1][lane];
+        const float omx = mg[MAX_NC + MAX_NC / 4][lane];
+        const float osum = mg[MAX_NC + MAX_NC / 4 + 1][lane];
         const float nm = fmaxf(mx, omx);
         sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) +
               (omx > -INFINITY ? osum * __expf(omx - nm) : 0.f);
@@ -670,7 +680,8 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
         for (int j = 0; j < NC; ++j) {
           const float y = mg[j][lane];
-          const int c = __float_as_int(mg[MAX_NC + j][lane]);
+          const uint32_t cb = (__float_as_uint(mg[MAX_NC + j / 4][lane]) >> (8 * (j & 3))) & 0xFFu;
+          const int c = (y > -INFINITY) ? static_cast<int>(cb) : -1;  // column 255 packs as 0xFF too
           if (__any_sync(0xffffffffu, y > top.v[NC - 1])) top.insert(y, c);
         }
       }
