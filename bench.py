@@ -316,6 +316,8 @@ def main():
                                         b["lse"].data_ptr(), L.ptr(prev_logp), L.ptr(prev_ids),
                                         b["ids"].data_ptr(), b["logp"].data_ptr(),
                                         b["nxt"].data_ptr(), b["parent"].data_ptr(), sptr))
+            if events is not None:
+                events[level][2].record(stream)
             cur, prev_logp, prev_ids = b["nxt"], b["logp"], b["ids"]
         if world > 1:
             dist.all_gather_into_tensor(gather_out[0], prev_ids)
@@ -330,7 +332,7 @@ def main():
     curs = [None] + [bufs[l]["nxt"].clone() for l in range(w.levels - 1)]
     costs = level_costs(w, dw, curs, wins)
 
-    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    ev = [[tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
            for _ in range(w.levels)] for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
@@ -379,6 +381,9 @@ def main():
     roof["tensor_frac"] = (tot_flops / t_step / 1e12) / tc_peak
     roof["hbm_frac"] = (tot_bytes / t_step / 1e9) / hbm_peak
     roof["per_level_ms"] = [round(x, 4) for x in lvl_ms]
+    roof["merge_ms"] = [round(statistics.mean(ev[s][l][1].elapsed_time(ev[s][l][2])
+                                              for s in range(args.steps)), 4)
+                        for l in range(w.levels)]
     roof["per_level_alg_bytes"] = [c[0] for c in costs]
     roof["per_level_alg_flops"] = [c[1] for c in costs]
     roof["roofline_ms"] = round(max(t_hbm, t_tc) * 1e3, 4)

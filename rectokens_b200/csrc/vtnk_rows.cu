@@ -205,8 +205,10 @@ mask_kernel(const T* __restrict__ logits, int64_t B, int64_t N, int64_t ls,
   }
 }
 
-// Beam merge: one warp per query.
-constexpr int kMergeWarps = 4;
+// Beam merge: one warp per query.  Candidate scores and tokens are staged in
+// shared memory; the k selection rounds touch only shared memory and
+// registers, then k lanes fetch the chosen candidates' nodes in parallel.
+constexpr int kMergeWarps = 8;
 
 __global__ void __launch_bounds__(kMergeWarps * 32)
 merge_kernel(const MergeArgs p) {
@@ -216,14 +218,19 @@ merge_kernel(const MergeArgs p) {
   const int64_t b = static_cast<int64_t>(blockIdx.x) * kMergeWarps + warp;
   if (b >= p.B) return;
   const int ncand = p.level == 0 ? p.n_cand : p.k * p.n_cand;
-  float* tot = msm + warp * p.cap;
-  int64_t* chosen = reinterpret_cast<int64_t*>(msm + kMergeWarps * p.cap) + warp * p.k;
+  // per warp: cap floats (scores) + cap ints (tokens) + k ints (choice) + k floats (score)
+  float* tot = msm + static_cast<size_t>(warp) * (2 * p.cap + 2 * p.k);
+  int* tok = reinterpret_cast<int*>(tot + p.cap);
+  int* sel = tok + p.cap;
+  float* selv = reinterpret_cast<float*>(sel + p.k);
+  const int64_t base = p.level == 0 ? b * p.n_cand : b * p.k * p.n_cand;
 
   for (int c = lane; c < ncand; c += 32) {
     const int64_t row = p.level == 0 ? b : b * p.k + c / p.n_cand;
-    const int64_t e = row * p.n_cand + c % p.n_cand;
-    const float lp = (p.cand_tok[e] >= 0) ? p.cand_logit[e] - p.row_lse[row] : -INFINITY;
+    const int64_t t = p.cand_tok[base + c];
+    const float lp = (t >= 0) ? p.cand_logit[base + c] - p.row_lse[row] : -INFINITY;
     tot[c] = p.level == 0 ? lp : p.prev_logp[row] + lp;
+    tok[c] = static_cast<int>(t);
   }
   __syncwarp();
   for (int r = 0; r < p.k; ++r) {
@@ -238,23 +245,27 @@ merge_kernel(const MergeArgs p) {
     }
     warp_argmax(bv, bc);
     if (lane == 0) {
-      const int64_t o = b * p.k + r;
-      const int64_t parent = p.level == 0 ? b : b * p.k + bc / p.n_cand;
-      const int64_t e = parent * p.n_cand + bc % p.n_cand;
-      p.out_logp[o] = bv;
-      p.out_node[o] = p.cand_node[e];
-      p.out_parent[o] = p.level == 0 ? b : parent;
-      p.out_ids[o * (p.level + 1) + p.level] = p.cand_tok[e];
-      chosen[r] = parent;
-      tot[bc] = __int_as_float(0x7fc00000);
+      sel[r] = bc;
+      selv[r] = bv;
+      tot[bc] = __int_as_float(0x7fc00000);  // taken
     }
     __syncwarp();
+  }
+  for (int r = lane; r < p.k; r += 32) {
+    const int bc = sel[r];
+    const int64_t o = b * p.k + r;
+    const int64_t parent = p.level == 0 ? b : b * p.k + bc / p.n_cand;
+    p.out_logp[o] = selv[r];
+    p.out_node[o] = p.cand_node[base + bc];
+    p.out_parent[o] = parent;
+    p.out_ids[o * (p.level + 1) + p.level] = tok[bc];
   }
   if (p.level > 0) {  // copy each new beam's history from its parent
     const int w = static_cast<int>(p.level);
     for (int t = lane; t < p.k * w; t += 32) {
       const int r = t / w, i = t % w;
-      p.out_ids[(b * p.k + r) * (w + 1) + i] = p.prev_ids[chosen[r] * w + i];
+      const int64_t parent = b * p.k + sel[r] / p.n_cand;
+      p.out_ids[(b * p.k + r) * (w + 1) + i] = p.prev_ids[parent * w + i];
     }
   }
 }
@@ -358,8 +369,7 @@ int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
 
 int launch_merge(const MergeArgs& p, cudaStream_t s) {
   if (p.B == 0) return VTNK_OK;
-  const size_t sm = static_cast<size_t>(kMergeWarps) * p.cap * sizeof(float) +
-                    static_cast<size_t>(kMergeWarps) * p.k * sizeof(int64_t);
+  const size_t sm = static_cast<size_t>(kMergeWarps) * (2 * p.cap + 2 * p.k) * sizeof(float);
   if (sm > 200 * 1024) {
     set_error("beams * candidates too large for the merge kernel");
     return VTNK_ERR_UNSUPPORTED;
