@@ -270,6 +270,140 @@ merge_kernel(const MergeArgs p) {
   }
 }
 
+// Beam merge, one thread per query (levels with at most 32 parent rows).
+// Every parent's candidate list is sorted (the beam step emits them by
+// descending logit, ties to the lower token) and a candidate's total
+// prev_logp + (logit - lse) is monotone within its list, so a query's k best
+// come from a k-way merge of its lists: each round takes the best list head
+// (ties to the lower flat candidate index) and advances that list.
+//   * A warp first stages its 32 queries' candidate logits (-inf where padded)
+//     in shared memory with coalesced loads, stride k*n+1 per query
+//     (conflict-free per-thread reads).
+//   * The selection rounds touch only shared memory and registers; every
+//     global read / write of the outputs is issued after them, together.
+//   * A query whose lists are not sorted (possible only for an arbitrary
+//     caller of vtnk_beam_merge) is merged by an exact successor scan instead.
+template <int KM>
+__global__ void __launch_bounds__(128)
+merge_sorted_kernel(const MergeArgs p) {
+  extern __shared__ float ssm[];
+  const int lane = threadIdx.x & 31;
+  const int n = p.n_cand;
+  const int L = p.level == 0 ? 1 : p.k;
+  const int per_q = L * n;
+  const int stride = per_q + 1;
+  float* st = ssm + static_cast<size_t>(threadIdx.x >> 5) * 32 * stride;
+  const int64_t qbase = static_cast<int64_t>(blockIdx.x) * blockDim.x + (threadIdx.x & ~31);
+  if (qbase >= p.B) return;  // warp-uniform
+  {
+    const int nq = static_cast<int>((p.B - qbase) < 32 ? (p.B - qbase) : 32);
+    const int total = nq * per_q;
+    const int64_t e0 = qbase * per_q;  // consecutive queries' candidates are contiguous
+    // flat index t -> (query, candidate) without division: walk t in steps
+    // of 32 and carry (q, c); 8 loads in flight per lane
+    int q = lane / per_q, c = lane - (lane / per_q) * per_q;
+    const int dq = 32 / per_q, dc = 32 - dq * per_q;
+#pragma unroll 8
+    for (int t = lane; t < total; t += 32) {
+      st[q * stride + c] = (p.cand_tok[e0 + t] >= 0) ? p.cand_logit[e0 + t] : -INFINITY;
+      q += dq;
+      c += dc;
+      if (c >= per_q) {
+        c -= per_q;
+        ++q;
+      }
+    }
+  }
+  __syncwarp();
+  const int64_t b = qbase + lane;
+  if (b >= p.B) return;
+  const float* my = st + lane * stride;
+  const int64_t row0 = p.level == 0 ? b : b * p.k;
+  bool sorted = true;
+  for (int i = 0; i < L; ++i)
+    for (int j = 1; j < n; ++j) sorted = sorted && !(my[i * n + j] > my[i * n + j - 1]);
+  float pv[KM], ls[KM], head[KM];
+  int pos[KM];
+#pragma unroll
+  for (int i = 0; i < KM; ++i) {
+    const bool in = i < L;
+    pv[i] = (in && p.level > 0) ? p.prev_logp[row0 + i] : 0.f;
+    ls[i] = in ? p.row_lse[row0 + i] : 0.f;
+    head[i] = in ? my[i * n] : -INFINITY;
+    pos[i] = 0;
+  }
+  // Chosen flat candidate and score per round (small per-thread arrays; the
+  // rounds are not unrolled, so these live in L1-cached local memory).
+  int sel_c[KM];
+  float sel_v[KM];
+  if (sorted) {
+#pragma unroll 1
+    for (int r = 0; r < p.k; ++r) {
+      float bv = -INFINITY;
+      int bc = INT_MAX, bi = 0;
+#pragma unroll
+      for (int i = 0; i < KM; ++i) {
+        if (i >= L || pos[i] >= n) continue;
+        const float lp = head[i] - ls[i];
+        const float v = p.level == 0 ? lp : pv[i] + lp;
+        const int c = i * n + pos[i];
+        if (v > bv || (v == bv && c < bc)) {
+          bv = v;
+          bc = c;
+          bi = i;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < KM; ++i)
+        if (i == bi) {
+          ++pos[i];
+          if (pos[i] < n) head[i] = my[i * n + pos[i]];
+        }
+      sel_c[r] = bc;
+      sel_v[r] = bv;
+    }
+  } else {
+    // successor scan: each round, the best candidate ordered after the previous pick
+    float prev_v = INFINITY;
+    int prev_c = -1;
+#pragma unroll 1
+    for (int r = 0; r < p.k; ++r) {
+      float bv = -INFINITY;
+      int bc = INT_MAX;
+#pragma unroll 1
+      for (int c = 0; c < per_q; ++c) {
+        const int i = c / n;
+        const float lv = my[c];
+        const float lp = lv > -INFINITY ? lv - p.row_lse[row0 + i] : -INFINITY;
+        const float v = p.level == 0 ? lp : p.prev_logp[row0 + i] + lp;
+        const bool after = v < prev_v || (v == prev_v && c > prev_c);
+        if (after && (v > bv || (v == bv && c < bc) || bc == INT_MAX)) {
+          bv = v;
+          bc = c;
+        }
+      }
+      prev_v = bv;
+      prev_c = bc;
+      sel_c[r] = bc;
+      sel_v[r] = bv;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < KM; ++r) {  // unrolled: the output loads of all rounds overlap
+    if (r >= p.k) break;
+    const int bi = sel_c[r] / n;
+    const int64_t parent = row0 + bi;
+    const int64_t e = parent * n + (sel_c[r] - bi * n);
+    const int64_t o = b * p.k + r;
+    p.out_logp[o] = sel_v[r];
+    p.out_node[o] = p.cand_node[e];
+    p.out_parent[o] = parent;
+    p.out_ids[o * (p.level + 1) + p.level] = p.cand_tok[e];
+    for (int t = 0; t < p.level; ++t)
+      p.out_ids[o * (p.level + 1) + t] = p.prev_ids[parent * p.level + t];
+  }
+}
+
 template <typename T>
 __global__ void synth_kernel(uint64_t key, int64_t e0, int64_t count, const T* __restrict__ table,
                              T* __restrict__ out) {
@@ -369,6 +503,27 @@ int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
 
 int launch_merge(const MergeArgs& p, cudaStream_t s) {
   if (p.B == 0) return VTNK_OK;
+  const int lists = p.level == 0 ? 1 : p.k;
+  const size_t per_warp = 32 * static_cast<size_t>(lists * p.n_cand + 1) * sizeof(float);
+  if (lists <= 32 && p.k <= 32 && 4 * per_warp <= 96 * 1024) {
+    const int grid = static_cast<int>((p.B + 127) / 128);
+    const size_t sm = 4 * per_warp;
+#define VTNK_MERGE_LAUNCH(KM)                                                                   \
+  do {                                                                                          \
+    if (sm > 48 * 1024)                                                                         \
+      cudaFuncSetAttribute(merge_sorted_kernel<KM>,                                             \
+                           cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));  \
+    merge_sorted_kernel<KM><<<grid, 128, sm, s>>>(p);                                           \
+  } while (0)
+    const int km = lists > p.k ? lists : p.k;
+    if (km <= 1) VTNK_MERGE_LAUNCH(1);
+    else if (km <= 4) VTNK_MERGE_LAUNCH(4);
+    else if (km <= 10) VTNK_MERGE_LAUNCH(10);
+    else if (km <= 16) VTNK_MERGE_LAUNCH(16);
+    else VTNK_MERGE_LAUNCH(32);
+#undef VTNK_MERGE_LAUNCH
+    return cuda_status(cudaGetLastError(), "merge_sorted_kernel launch");
+  }
   const size_t sm = static_cast<size_t>(kMergeWarps) * (2 * p.cap + 2 * p.k) * sizeof(float);
   if (sm > 200 * 1024) {
     set_error("beams * candidates too large for the merge kernel");
