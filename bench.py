@@ -258,6 +258,7 @@ def main():
     torch.cuda.set_device(dev)
 
     from rectokens_b200 import workload as WL
+    from rectokens_b200.distributed import gather_results
     from rectokens_b200.decoding.beam_search import (
         beam_merge,
         beam_step,
@@ -320,9 +321,7 @@ def main():
                 events[level][2].record(stream)
             cur, prev_logp, prev_ids = b["nxt"], b["logp"], b["ids"]
         if world > 1:
-            dist.all_gather_into_tensor(gather_out[0], prev_ids)
-            dist.all_gather_into_tensor(gather_out[1], prev_logp)
-            dist.all_gather_into_tensor(gather_out[2], cur)
+            gather_results(prev_ids, prev_logp, cur, out=gather_out)
         return cur
 
     # warm-up (also records the per-level node arrays for the cost model)

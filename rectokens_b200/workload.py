@@ -71,18 +71,16 @@ class DeviceWorkload:
 def make_device_workload(w: S.Workload, device, shard: int = 0, n_shards: int = 1,
                          trie: CompactCSRTrie | None = None) -> DeviceWorkload:
     """Shard ``shard`` of ``n_shards`` (contiguous query ranges) of workload ``w``."""
-    if w.batch % n_shards:
-        raise ValueError("batch must divide evenly across shards")
-    bq = w.batch // n_shards
-    q0 = shard * bq
+    from rectokens_b200.distributed import level_rows, shard_queries
+
+    q0, bq = shard_queries(w.batch, shard, n_shards)
     dtype = torch.float32 if w.dtype == "f32" else torch.bfloat16
     if trie is None:
         trie = build_trie(w, device)
     weight = head_weight(w, device)
     hidden, offs = [], []
     for level in range(w.levels):
-        per_q = 1 if level == 0 else w.beams
-        r0, rows = q0 * per_q, bq * per_q
+        r0, rows = level_rows(q0, bq, level, w.beams)
         hidden.append(synth_hidden(w.seed, level, r0, rows, w.hidden, dtype, device))
         offs.append(r0)
     return DeviceWorkload(w, trie, weight, hidden, offs, bq)

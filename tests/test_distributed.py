@@ -1,0 +1,82 @@
+"""Batch sharding + all-gather of the beam search (CPU, two gloo ranks).
+
+Each rank searches its contiguous query shard with the CPU oracle, using the
+hidden states of its global rows; the gathered result must equal the
+single-process search of the whole batch (the GPU bench does the same with the
+CUDA search and NCCL)."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from rectokens_b200 import distributed as D
+from rectokens_b200 import synthetic as S
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _inputs(w, q0, nq):
+    hid = []
+    for level in range(w.levels):
+        r0, rows = D.level_rows(q0, nq, level, w.beams)
+        hid.append(S.hidden_f32(w.seed, level, r0, rows, w.hidden))
+    return hid
+
+
+def _worker(rank, world, port, q):
+    from oracle import vtnk_oracle as O
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        w = S.WORKLOADS["cfg1"]
+        w = type(w)(**{**w.__dict__, "batch": 8})
+        tok = S.to_tokens(w.make_catalog(), w.codes)
+        rp, cv, lmb, _, _ = O.build_sorted_csr(tok, w.vocab, 1)
+        W = S.head_f32(w.seed, w.vocab, w.hidden)
+        q0, nq = D.shard_queries(w.batch, rank, world)
+        ids, logp, node = O.beam_search(_inputs(w, q0, nq), W, rp, cv, lmb, nq, w.beams, w.topk)
+        out = D.gather_results(torch.from_numpy(ids.reshape(nq * w.beams, -1)),
+                               torch.from_numpy(logp), torch.from_numpy(node))
+        if rank == 0:
+            full = O.beam_search(_inputs(w, 0, w.batch), W, rp, cv, lmb, w.batch, w.beams, w.topk)
+            q.put((out[0].numpy(), out[1].numpy(), out[2].numpy(),
+                   full[0].reshape(w.batch * w.beams, -1), full[1], full[2]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_search_equals_single_process():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    g_ids, g_logp, g_node, f_ids, f_logp, f_node = res
+    np.testing.assert_array_equal(g_ids, f_ids)
+    np.testing.assert_array_equal(g_node, f_node)
+    np.testing.assert_allclose(g_logp, f_logp, rtol=0, atol=1e-6)
+
+
+def test_shard_arithmetic():
+    assert D.shard_queries(65536, 3, 8) == (24576, 8192)
+    assert D.level_rows(24576, 8192, 0, 10) == (24576, 8192)
+    assert D.level_rows(24576, 8192, 2, 10) == (245760, 81920)
+    with pytest.raises(ValueError):
+        D.shard_queries(10, 0, 3)
