@@ -81,6 +81,14 @@ class ClockSampler:
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        if not self.lines:  # very short timed region: take one reading now
+            try:
+                r = subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}",
+                                    "--format=csv,noheader,nounits", "-i", str(self.gpu)],
+                                   capture_output=True, text=True, timeout=10)
+                self.lines += r.stdout.strip().splitlines()
+            except (OSError, subprocess.TimeoutExpired):
+                pass
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -324,8 +332,18 @@ def main():
             gather_results(prev_ids, prev_logp, cur, out=gather_out)
         return cur
 
-    # warm-up (also records the per-level node arrays for the cost model)
-    for _ in range(max(3, args.warmup)):
+    # warm-up (also records the per-level node arrays for the cost model); the
+    # clock sampler starts before the last warm-up searches so that it is
+    # running when the timed region begins
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = vis.split(",")[local] if vis and vis.split(",")[local].strip().isdigit() else local
+    clocks = ClockSampler(int(phys))
+    n_warm = max(3, args.warmup)
+    for i in range(n_warm):
+        if i == n_warm - 2:
+            torch.cuda.synchronize(dev)
+            clocks.start()
+            time.sleep(0.3)
         one_search()
     torch.cuda.synchronize(dev)
     curs = [None] + [bufs[l]["nxt"].clone() for l in range(w.levels - 1)]
@@ -334,13 +352,9 @@ def main():
     ev = [[tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
            for _ in range(w.levels)] for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
-    phys = vis.split(",")[local] if vis and vis.split(",")[local].strip().isdigit() else local
-    clocks = ClockSampler(int(phys))
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
-    clocks.start()
     t_start.record(stream)
     for s in range(args.steps):
         one_search(ev[s])
