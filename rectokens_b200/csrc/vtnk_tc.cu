@@ -344,9 +344,15 @@ struct TopN {
   // Branch-free insert: a value not above the current n-th largest gets
   // pos == NC and leaves the list unchanged.
   __device__ __forceinline__ void insert(float x, int col) {
-    int pos = 0;
+    // position = number of entries >= x, summed as a balanced tree
+    int ge[NC];
 #pragma unroll
-    for (int i = 0; i < NC; ++i) pos += (v[i] >= x) ? 1 : 0;
+    for (int i = 0; i < NC; ++i) ge[i] = (v[i] >= x) ? 1 : 0;
+#pragma unroll
+    for (int w = 1; w < NC; w <<= 1)
+#pragma unroll
+      for (int i = 0; i + w < NC; i += 2 * w) ge[i] += ge[i + w];
+    const int pos = ge[0];
 #pragma unroll
     for (int i = NC - 1; i > 0; --i) {
       v[i] = (i > pos) ? v[i - 1] : ((i == pos) ? x : v[i]);
@@ -626,15 +632,17 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #ifdef VTNK_TC_EXPERIMENT_NOSELECT
         pend = 0u;  // tuning experiment only: measures the pipeline without top-n work
 #endif
-        while (__any_sync(0xffffffffu, pend != 0u)) {
-          float y = -INFINITY;
-          int col = 0;
-          if (pend) {
-            const int i = __ffs(pend) - 1;
-            pend &= pend - 1;
-            y = sx[i * 32 + lane];
-            col = chunk * 32 + i;
-          }
+        // software-pipelined: the next candidate's shared-memory read overlaps
+        // the current insert
+        int inext = pend ? __ffs(pend) - 1 : -1;
+        pend &= pend - 1;
+        float ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
+        while (__any_sync(0xffffffffu, inext >= 0)) {
+          const float y = ynext;
+          const int col = chunk * 32 + inext;
+          inext = pend ? __ffs(pend) - 1 : -1;
+          pend &= pend - 1;
+          ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
           top.insert(y, col);  // no-op for -inf / values no longer above the n-th best
         }
         __syncwarp();
