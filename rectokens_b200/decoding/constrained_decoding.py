@@ -1,0 +1,184 @@
+"""Drop-in beam-search driver for language models that return full logits.
+
+Same entry points and semantics as the reference's
+``rectokens.decoding.constrained_decoding`` (``autoregressive_generate``
+:140-179, ``decode_one_step`` :194-398, route A: the model computes logits over
+the whole vocabulary and the CSR trie masks them).  Per level:
+
+* dense levels (``step < len(trie.dense_mask_by_layer)``): the dense mask, as
+  in the reference (:261-268);
+* CSR levels: the CUDA mask op ``constrained_node_transition``;
+* candidates: ``topk(beam_size)`` of the masked logits with their
+  log-softmax (:294-303; temperature > 0 samples with ``torch.multinomial``
+  exactly as the reference does);
+* beam merge and next trie node: the CUDA merge kernel (``vtnk_beam_merge``),
+  which also returns the parent row of every new beam; the child node of each
+  candidate is found on the device by matching its token against the parent's
+  ``valid_idxs`` (:372-383) -- no boolean-mask indexing, so no host
+  synchronisation per level;
+* KV cache and attention mask are reordered by the parent rows (:305-366).
+
+The ``attr_path`` / ``SparseLinear`` route of the reference passes the weight
+untransposed to the fused op (rectokens/modules/sparse_linear.py:56-94) and is
+not reproduced; use ``rectokens_b200.constrained_beam_search`` for the fused
+hidden-state path.
+"""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+from rectokens_b200 import _lib as L
+from rectokens_b200.ops.constrained_node_transition import constrained_node_transition
+from rectokens_b200.schemas.compact_csr_trie import CompactCSRTrie
+from rectokens_b200.schemas.config import GenerationConfig
+from rectokens_b200.schemas.state import (
+    ConstrainedGenerationState,
+    ConstraintState,
+    GenerationState,
+)
+
+
+def _reindex_past_key_values(past_key_values, indices: torch.Tensor):
+    """Reorder a KV cache along the batch axis (reference :182-191)."""
+    if past_key_values is None:
+        return None
+    if hasattr(past_key_values, "reorder_cache"):
+        past_key_values.reorder_cache(indices)
+        return past_key_values
+    return tuple((k.index_select(0, indices), v.index_select(0, indices))
+                 for k, v in past_key_values)
+
+
+def _merge(level, B, k, tok, logit, node, lse, prev_logp, prev_ids):
+    n = tok.shape[1]
+    dev = tok.device
+    ids = torch.empty((B * k, level + 1), dtype=torch.int64, device=dev)
+    logp = torch.empty((B * k,), dtype=torch.float32, device=dev)
+    nxt = torch.empty((B * k,), dtype=torch.int64, device=dev)
+    parent = torch.empty((B * k,), dtype=torch.int64, device=dev)
+    tok, logit, node, lse = (t.contiguous() for t in (tok, logit, node, lse))
+    L.check(L.lib().vtnk_beam_merge(
+        level, B, k, n, tok.data_ptr(), logit.data_ptr(), node.data_ptr(), lse.data_ptr(),
+        L.ptr(prev_logp), L.ptr(prev_ids), ids.data_ptr(), logp.data_ptr(), nxt.data_ptr(),
+        parent.data_ptr(), L.stream_of(dev)))
+    return ids, logp, nxt, parent
+
+
+@torch.inference_mode()
+def decode_one_step(
+    constrained_generation_state: ConstrainedGenerationState,
+    model_fwd: nn.Module,
+    input_ids: torch.Tensor,
+    attention_mask: Optional[torch.Tensor] = None,
+) -> ConstrainedGenerationState:
+    """One constrained beam-search level (reference constrained_decoding.py:194-398)."""
+    assert input_ids.ndim == 2
+    cs = constrained_generation_state.constraint_state
+    trie, step = cs.trie, cs.step
+    gen = constrained_generation_state.generation_state
+    config = constrained_generation_state.generation_config
+    k, beam_size = config.k, config.beam_size
+    first = gen is None
+    if first:
+        past_key_values, log_probas = None, None
+    else:
+        past_key_values, log_probas = gen.past_key_values, gen.log_probas
+        attention_mask = gen.attention_mask
+
+    out = model_fwd(input_ids, past_key_values=past_key_values, attention_mask=attention_mask,
+                    use_cache=True)
+    logits = out.logits[:, -1, :]
+    new_past = out.past_key_values
+    R = logits.shape[0]
+    B = R if first else R // k
+    prev_ids = None if first else gen.generated_ids.reshape(B * k, -1)
+    n_dense = len(trie.dense_mask_by_layer)
+
+    next_nodes = valid_idxs = None
+    if step < n_dense:
+        layer_mask = trie.dense_mask_by_layer[step]
+        if first:
+            layer_mask = layer_mask.unsqueeze(0).expand(R, -1)
+        else:
+            layer_mask = layer_mask[prev_ids.unbind(-1)]
+        masked = logits.float().masked_fill(~layer_mask, float("-inf"))
+    else:
+        next_nodes, valid_idxs, masked = constrained_node_transition(logits, cs)
+        masked = masked.float()
+
+    lse = torch.logsumexp(masked, dim=-1)
+    if config.temperature == 0.0:
+        cand_logit, cand_tok = masked.topk(beam_size, dim=-1)
+    else:
+        probs = F.softmax(masked / config.temperature, dim=-1)
+        cand_tok = torch.multinomial(probs, num_samples=beam_size)
+        cand_logit = masked.gather(1, cand_tok)
+        # sampled candidates are unsorted; the merge takes its exact path for them
+    cand_tok = torch.where(cand_logit > float("-inf"), cand_tok, torch.full_like(cand_tok, -1))
+
+    if next_nodes is not None:
+        # child node of each candidate: the branch slot whose token matches
+        # (per-row sort + binary search; padding sorts last)
+        vi = torch.where(valid_idxs >= 0, valid_idxs, torch.iinfo(torch.int64).max)
+        vs, perm = torch.sort(vi, dim=1)
+        pos = torch.searchsorted(vs, cand_tok).clamp(max=vs.shape[1] - 1)
+        hit = vs.gather(1, pos) == cand_tok
+        slot = perm.gather(1, pos)
+        cand_node = torch.where(hit & (cand_tok >= 0), next_nodes.gather(1, slot), -1)
+    else:
+        cand_node = torch.full_like(cand_tok, -1)
+
+    if config.temperature != 0.0:
+        # the reference scores sampled candidates by log(p_T) (:298-303)
+        cand_logit = torch.where(cand_tok >= 0, cand_logit / config.temperature, cand_logit)
+        lse = torch.logsumexp(masked / config.temperature, dim=-1)
+
+    ids, new_logp, nxt, parent = _merge(step, B, k, cand_tok, cand_logit.float(), cand_node,
+                                        lse.float(), log_probas, prev_ids)
+    new_past = _reindex_past_key_values(new_past, parent)
+    if attention_mask is not None:
+        attention_mask = torch.cat(
+            [attention_mask.index_select(0, parent),
+             torch.ones(B * k, 1, dtype=attention_mask.dtype, device=attention_mask.device)],
+            dim=1)
+    if step == n_dense - 1:
+        nxt = trie.dense_states[ids.unbind(-1)]
+    elif step < n_dense - 1:
+        nxt = None
+    return ConstrainedGenerationState(
+        generation_config=config,
+        generation_state=GenerationState(generated_ids=ids.reshape(B, k, -1),
+                                         past_key_values=new_past, log_probas=new_logp,
+                                         attention_mask=attention_mask),
+        constraint_state=ConstraintState(step=step + 1, trie=trie, cur_node=nxt),
+    )
+
+
+@torch.inference_mode()
+def autoregressive_generate(
+    model: nn.Module,
+    trie: CompactCSRTrie,
+    input_ids: torch.Tensor,
+    generation_config: GenerationConfig,
+    attr_path: Optional[str] = None,
+    attention_mask: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """Constrained generation for ``generation_config.steps`` levels; returns
+    ``generated_ids`` ``(B, k, steps)`` (reference :140-179)."""
+    if attr_path is not None:
+        raise NotImplementedError(
+            "the SparseLinear route is not reproduced; use constrained_beam_search")
+    state = ConstrainedGenerationState(
+        generation_config=generation_config, generation_state=None,
+        constraint_state=ConstraintState(step=0, trie=trie, cur_node=None))
+    for _ in range(generation_config.steps):
+        state = decode_one_step(state, model, input_ids, attention_mask)
+        g = state.generation_state.generated_ids
+        input_ids = g.reshape(-1, g.shape[-1])[:, -1:]
+        attention_mask = None
+    return state.generation_state.generated_ids
