@@ -404,6 +404,118 @@ merge_sorted_kernel(const MergeArgs p) {
   }
 }
 
+// Beam merge, one group of G lanes per query (G = 16 or 32, k <= G lists):
+// lane i owns parent list i.  Lists are sorted (descending logit), so each
+// round is a G-lane argmax over the list heads (ties to the lower flat
+// candidate index) and the winning lane advances its head; lane r keeps
+// round r's choice and writes output beam r.  Candidates are staged in shared
+// memory by coalesced loads of the block's queries.  A query with an
+// unsorted list is merged by its lane 0 with the exact successor scan.
+template <int G>
+__global__ void __launch_bounds__(128)
+merge_group_kernel(const MergeArgs p) {
+  extern __shared__ float gsm[];
+  constexpr int QPB = 128 / G;  // queries per block
+  const int n = p.n_cand;
+  const int L = p.level == 0 ? 1 : p.k;
+  const int per_q = L * n;
+  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * QPB;
+  {
+    const int64_t nq64 = p.B - q0 < QPB ? p.B - q0 : QPB;
+    const int total = static_cast<int>(nq64) * per_q;
+    const int64_t e0 = q0 * per_q;
+    for (int t = threadIdx.x; t < total; t += 128)
+      gsm[t] = (p.cand_tok[e0 + t] >= 0) ? p.cand_logit[e0 + t] : -INFINITY;
+  }
+  __syncthreads();
+  const int g = threadIdx.x / G;        // query slot in the block
+  const int li = threadIdx.x % G;       // list (parent) index
+  const int64_t b = q0 + g;
+  if (b >= p.B) return;                 // whole groups retire together
+  const unsigned gmask = (G == 32) ? 0xffffffffu : (0xffffu << ((threadIdx.x & 31) & 16));
+  const float* my = gsm + g * per_q;
+  const int64_t row0 = p.level == 0 ? b : b * p.k;
+  const bool has = li < L;
+  const float pv = (has && p.level > 0) ? p.prev_logp[row0 + li] : 0.f;
+  const float ls = has ? p.row_lse[row0 + li] : 0.f;
+  bool ok = true;
+  if (has)
+    for (int j = 1; j < n; ++j) ok = ok && !(my[li * n + j] > my[li * n + j - 1]);
+  const bool sorted = __all_sync(gmask, ok);
+  int pos = 0;
+  int my_c = 0;
+  float my_v = -INFINITY;
+  if (sorted) {
+    for (int r = 0; r < p.k; ++r) {
+      float v = -INFINITY;
+      int c = INT_MAX;
+      if (has && pos < n) {
+        const float lp = my[li * n + pos] - ls;
+        v = p.level == 0 ? lp : pv + lp;
+        c = li * n + pos;
+      }
+#pragma unroll
+      for (int o = G / 2; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(gmask, v, o);
+        const int oc = __shfl_xor_sync(gmask, c, o);
+        if (ov > v || (ov == v && oc < c)) {
+          v = ov;
+          c = oc;
+        }
+      }
+      if (has && c == li * n + pos) ++pos;  // the winning list advances
+      if (li == r) {
+        my_c = c;
+        my_v = v;
+      }
+    }
+  } else if (li == 0) {
+    // exact successor scan for this query; lane 0 writes all k outputs below
+    float prev_v = INFINITY;
+    int prev_c = -1;
+    for (int r = 0; r < p.k; ++r) {
+      float bv = -INFINITY;
+      int bc = INT_MAX;
+      for (int c = 0; c < per_q; ++c) {
+        const int i = c / n;
+        const float lv = my[c];
+        const float lp = lv > -INFINITY ? lv - p.row_lse[row0 + i] : -INFINITY;
+        const float v = p.level == 0 ? lp : p.prev_logp[row0 + i] + lp;
+        const bool after = v < prev_v || (v == prev_v && c > prev_c);
+        if (after && (v > bv || (v == bv && c < bc) || bc == INT_MAX)) {
+          bv = v;
+          bc = c;
+        }
+      }
+      prev_v = bv;
+      prev_c = bc;
+      const int bi = bc / n;
+      const int64_t parent = row0 + bi;
+      const int64_t e = parent * n + (bc - bi * n);
+      const int64_t o = b * p.k + r;
+      p.out_logp[o] = bv;
+      p.out_node[o] = p.cand_node[e];
+      p.out_parent[o] = parent;
+      p.out_ids[o * (p.level + 1) + p.level] = p.cand_tok[e];
+      for (int t = 0; t < p.level; ++t)
+        p.out_ids[o * (p.level + 1) + t] = p.prev_ids[parent * p.level + t];
+    }
+    return;
+  }
+  if (!sorted || li >= p.k) return;
+  const int r = li;
+  const int bi = my_c / n;
+  const int64_t parent = row0 + bi;
+  const int64_t e = parent * n + (my_c - bi * n);
+  const int64_t o = b * p.k + r;
+  p.out_logp[o] = my_v;
+  p.out_node[o] = p.cand_node[e];
+  p.out_parent[o] = parent;
+  p.out_ids[o * (p.level + 1) + p.level] = p.cand_tok[e];
+  for (int t = 0; t < p.level; ++t)
+    p.out_ids[o * (p.level + 1) + t] = p.prev_ids[parent * p.level + t];
+}
+
 template <typename T>
 __global__ void synth_kernel(uint64_t key, int64_t e0, int64_t count, const T* __restrict__ table,
                              T* __restrict__ out) {
@@ -504,6 +616,25 @@ int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
 int launch_merge(const MergeArgs& p, cudaStream_t s) {
   if (p.B == 0) return VTNK_OK;
   const int lists = p.level == 0 ? 1 : p.k;
+  if (p.k <= 32 && p.level > 0) {  // one list per query at level 0: thread-per-query below
+    const int G = p.k <= 16 ? 16 : 32;
+    const size_t sm = static_cast<size_t>(128 / G) * lists * p.n_cand * sizeof(float);
+    if (sm <= 96 * 1024) {
+      const int grid = static_cast<int>((p.B + 128 / G - 1) / (128 / G));
+      if (G == 16) {
+        if (sm > 48 * 1024)
+          cudaFuncSetAttribute(merge_group_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(sm));
+        merge_group_kernel<16><<<grid, 128, sm, s>>>(p);
+      } else {
+        if (sm > 48 * 1024)
+          cudaFuncSetAttribute(merge_group_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(sm));
+        merge_group_kernel<32><<<grid, 128, sm, s>>>(p);
+      }
+      return cuda_status(cudaGetLastError(), "merge_group_kernel launch");
+    }
+  }
   const size_t per_warp = 32 * static_cast<size_t>(lists * p.n_cand + 1) * sizeof(float);
   if (lists <= 32 && p.k <= 32 && 4 * per_warp <= 96 * 1024) {
     const int grid = static_cast<int>((p.B + 127) / 128);
