@@ -58,6 +58,10 @@ constexpr int PAIR_M = 2 * BM;  // rows per CTA pair (one cta_group::2 MMA tile)
 #define VTNK_TC_STAGES 5
 #endif
 constexpr int STAGES = VTNK_TC_STAGES;
+// Column groups of the epilogue's lower bound (16 or 32; 32 whenever NC > 16).
+#ifndef VTNK_TC_GROUPS
+#define VTNK_TC_GROUPS 32
+#endif
 constexpr int A_BYTES = BM * BK * 2;        // this CTA's 128 rows
 constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's half of the 256 window rows
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -375,6 +379,53 @@ __device__ __forceinline__ float tree_max(const float (&x)[N]) {
   return t[0];
 }
 
+// The K-th largest of N values (N a power of two): bitonic sort, descending.
+template <int N, int K>
+__device__ __forceinline__ float nth_largest(float (&a)[N]) {
+  if constexpr (K == N) {
+    float t = a[0];
+#pragma unroll
+    for (int i = 1; i < N; ++i) t = fminf(t, a[i]);
+    return t;
+  } else if constexpr (K == 1) {
+    return tree_max<N>(a);
+  } else {
+#pragma unroll
+    for (int k = 2; k <= N; k <<= 1)
+#pragma unroll
+      for (int j = k >> 1; j > 0; j >>= 1)
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+          const int l = i ^ j;
+          if (l > i) {
+            const float hi = fmaxf(a[i], a[l]), lo = fminf(a[i], a[l]);
+            const bool desc = (i & k) == 0;
+            a[i] = desc ? hi : lo;
+            a[l] = desc ? lo : hi;
+          }
+        }
+    return a[K - 1];
+  }
+}
+
+// One 32-column chunk of this warp's 32 rows from TMEM (warp-collective):
+// the child mask applied (non-children are -inf) and the bias added.
+__device__ __forceinline__ void load_chunk(uint32_t taddr, int chunk, const uint32_t (&m)[BN / 32],
+                                           bool has_bias, const float* sbias, float (&x)[32]) {
+  uint32_t v[32];
+  __syncwarp();
+  tmem_ld32(taddr + chunk * 32, v);
+  uint32_t mw = 0;
+#pragma unroll
+  for (int i = 0; i < BN / 32; ++i) mw = (i == chunk) ? m[i] : mw;
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float y = __uint_as_float(v[i]);
+    if (has_bias) y += sbias[chunk * 32 + i];
+    x[i] = ((mw >> i) & 1u) ? y : -INFINITY;
+  }
+}
+
 // Exact per-row path for a row whose node is outside the index or whose
 // children are not a clean sorted in-window set (slow, never taken for a
 // sorted catalog trie queried at the right depth).
@@ -587,25 +638,27 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       float mx = -INFINITY, sum = 0.f;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BN;
       const bool has_bias = p.bias != nullptr;
-#pragma unroll 1
-      for (int chunk = half * (BN / 64); chunk < (half + 1) * (BN / 64); ++chunk) {
-        uint32_t v[32];
-        __syncwarp();
-        PROF_T0(t_ld);
-        tmem_ld32(taddr + chunk * 32, v);  // warp-collective: every lane, every chunk
-        PROF_ACC(pe_ld, t_ld);
-        uint32_t mw = 0;
+      const int c0 = half * (BN / 64);  // this warp's first 32-column chunk
+      // Pass 1 over the accumulator: online log-sum-exp, and the maxima of G
+      // column groups (column j of the half in group j % G).  The NC-th largest
+      // group maximum is a lower bound of the NC-th largest value (the NC
+      // largest group maxima are NC distinct entries), so pass 2 only inserts
+      // values at or above it.
+      constexpr int G = NC <= VTNK_TC_GROUPS ? VTNK_TC_GROUPS : 32;
+      float gm[G];
 #pragma unroll
-        for (int i = 0; i < BN / 32; ++i) mw = (i == chunk) ? m[i] : mw;
+      for (int g = 0; g < G; ++g) gm[g] = -INFINITY;
+      float cmax[BN / 64];
+#pragma unroll
+      for (int ci = 0; ci < BN / 64; ++ci) {
+        const int chunk = c0 + ci;
         float x[32];
+        load_chunk(taddr, chunk, m, has_bias, S.bias, x);
+        const float cm = tree_max<32>(x);
+        cmax[ci] = cm;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float y = __uint_as_float(v[i]);
-          if (has_bias) y += S.bias[chunk * 32 + i];
-          x[i] = ((mw >> i) & 1u) ? y : -INFINITY;
-        }
-        // online log-sum-exp over the chunk's children
-        const float nm = fmaxf(mx, tree_max<32>(x));
+        for (int i = 0; i < 32; ++i) gm[i % G] = fmaxf(gm[i % G], x[i]);
+        const float nm = fmaxf(mx, cm);
         sum *= (nm == mx) ? 1.f : __expf(mx - nm);
         mx = nm;
         float e[32];
@@ -616,16 +669,25 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
           for (int i = 0; i < w; ++i) e[i] += e[i + w];
         sum += e[0];
-        // top-n: each lane inserts only its values above its current n-th best,
-        // in column order (ties keep the lower column); the warp loops
-        // max-over-lanes(candidates) times.  Values are read back from shared
-        // memory ([col][lane]: conflict-free for any per-lane column).
+      }
+      const float lb = nth_largest<G, NC>(gm);
+      // Pass 2: top-n in column order over the values >= lb.  Each lane
+      // inserts only its values above its current n-th best; the warp loops
+      // max-over-lanes(candidates) times.  Values are read back from shared
+      // memory ([col][lane]: conflict-free for any per-lane column).
+      float* sx = &S.chunk_x[warp - 2][0][0];
+#pragma unroll 1
+      for (int ci = 0; ci < BN / 64; ++ci) {
+        if (!__any_sync(0xffffffffu, cmax[ci] >= lb && cmax[ci] > -INFINITY)) continue;
+        const int chunk = c0 + ci;
+        float x[32];
+        load_chunk(taddr, chunk, m, has_bias, S.bias, x);
         const float thr = top.v[NC - 1];
         uint32_t pend = 0;
-        float* sx = &S.chunk_x[warp - 2][0][0];
+        __syncwarp();
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          pend |= (x[i] > thr) ? (1u << i) : 0u;
+          pend |= (x[i] > thr && x[i] >= lb) ? (1u << i) : 0u;
           sx[i * 32 + lane] = x[i];
         }
         __syncwarp();
@@ -645,8 +707,8 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
           top.insert(y, col);  // no-op for -inf / values no longer above the n-th best
         }
-        __syncwarp();
       }
+      __syncwarp();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);  // the leader's MMA may reuse it
