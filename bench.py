@@ -142,7 +142,8 @@ def level_costs(w, dw, curs, wins):
         bytes_ = (rows * w.hidden * es                       # hidden states
                   + uniq.numel() * 16 + kids_unique * 16     # CSR rows touched (row_ptr pair, col+val)
                   + wins[level][1] * w.hidden * es           # level head slice
-                  + rows * w.topk * (4 + 8 + 8) + rows * 4)  # candidates + row lse
+                  + (rows * (4 + 8) if w.sampling                  # sample + node
+                     else rows * w.topk * (4 + 8 + 8) + rows * 4))  # candidates + row lse
         flops = 2 * w.hidden * kids_rows
         out.append((bytes_, flops))
     return out
@@ -170,6 +171,20 @@ class CpuBaseline:
             return S.hidden_f32(w.seed, level, r0, rows, w.hidden)
         return S.bf16_bits_to_f32(S.hidden_bits(w.seed, level, r0, rows, w.hidden))
 
+    def _sample_search(self, hidden, q0):
+        """The reference's sampling op level by level (kernels:562-783): Gumbel
+        noise at the rows' global offsets, argmax, next node of the sample."""
+        O, w = self.O, self.w
+        cur = np.zeros(hidden[0].shape[0], dtype=np.int64)
+        for level, a in enumerate(hidden):
+            mb = self.lmb[level]
+            noise = O.gumbel_noise(w.seed, a.shape[0], mb, row0=q0)
+            nn, _, smp, score = O.fused_sampling(a, self.W.T, None, self.rp, self.cv, cur, mb,
+                                                 noise, w.temperature, acc=np.float32)
+            best = np.argmax(score, axis=1)
+            cur = np.where(smp >= 0, nn[np.arange(nn.shape[0]), best], -1)
+        return cur
+
     def rows(self, nq):
         return nq * (1 + self.w.beams * (self.w.levels - 1))
 
@@ -181,8 +196,11 @@ class CpuBaseline:
         inputs = {c: [self._hidden(l, *c) for l in range(w.levels)] for c in chunks}
 
         def one(c):
-            self.O.beam_search(inputs[c], self.W, self.rp, self.cv, self.lmb, c[1], w.beams,
-                               w.topk, acc=np.float32)
+            if w.sampling:
+                self._sample_search(inputs[c], c[0])
+            else:
+                self.O.beam_search(inputs[c], self.W, self.rp, self.cv, self.lmb, c[1], w.beams,
+                                   w.topk, acc=np.float32)
 
         t0 = time.perf_counter()
         with ThreadPoolExecutor(max_workers=threads) as ex:
@@ -218,13 +236,19 @@ def main():
 
         w = dataclasses.replace(w, batch=args.batch)
     workload_cfg = {
-        "workload": f"{args.workload}: {w.levels}-level beam search, catalog K={w.codes} "
-                    f"L={w.levels}, H={w.hidden} {w.dtype} head, batch {w.batch} x {w.beams} "
-                    f"beams, top-{w.topk}",
+        "workload": (f"{args.workload}: {w.levels}-level Gumbel-max sampled search "
+                     f"(T={w.temperature}, Philox seed {w.seed}), catalog K={w.codes} "
+                     f"L={w.levels}, H={w.hidden} {w.dtype} head, batch {w.batch}"
+                     if w.sampling else
+                     f"{args.workload}: {w.levels}-level beam search, catalog K={w.codes} "
+                     f"L={w.levels}, H={w.hidden} {w.dtype} head, batch {w.batch} x {w.beams} "
+                     f"beams, top-{w.topk}"),
         "global_batch": w.batch, "beams": w.beams, "topk": w.topk, "levels": w.levels,
         "hidden": w.hidden, "rows_per_search": S.search_rows(w),
         "parallelism": f"dp{args.gpus}" if args.gpus > 1 else "single",
-        "l2": "inputs larger than L2 (hidden states >= 0.47 GB per level), no flush",
+        "l2": ("hidden states of a level (29 MB) fit in L2: a 256 MB buffer is written "
+               "between timed searches" if w.sampling else
+               "inputs larger than L2 (hidden states >= 0.47 GB per level), no flush"),
     }
 
     if args.impl == "reference":
@@ -271,6 +295,7 @@ def main():
         beam_merge,
         beam_step,
         constrained_beam_search_from_host,
+        constrained_sampling_search,
         child_index,
         level_windows,
     )
@@ -307,7 +332,33 @@ def main():
                       torch.empty((w.batch * k,), dtype=torch.float32, device=dev),
                       torch.empty((w.batch * k,), dtype=torch.int64, device=dev))
 
-    def one_search(events=None):
+    temp_t = torch.tensor([w.temperature], dtype=torch.float32, device=dev)
+    samp_out = [(torch.empty((R,), dtype=torch.float32, device=dev),
+                 torch.empty((R,), dtype=torch.int64, device=dev)) for R in rows_l]
+    flush = torch.empty((256 << 20,), dtype=torch.uint8, device=dev) if w.sampling else None
+
+    def one_sampled(events=None):
+        cur = None
+        for level in range(w.levels):
+            smp, nd = samp_out[level]
+            if events is not None:
+                events[level][0].record(stream)
+            L.check(lib.vtnk_fused_linear_constrained_node_transition_sampling_ix(
+                lins[level], L.ptr(cur), csr, dw.trie.layer_max_branches[level], w.seed,
+                temp_t.data_ptr(), idxs[level], None, None, smp.data_ptr(), nd.data_ptr(), sptr))
+            if events is not None:
+                events[level][1].record(stream)
+                events[level][2].record(stream)
+            cur = nd
+        return cur
+
+    def one_search(events=None, flush_ev=None):
+        if w.sampling:
+            if flush_ev is not None:  # L2 flush between timed searches, timed and subtracted
+                flush_ev[0].record(stream)
+                flush.fill_(1)
+                flush_ev[1].record(stream)
+            return one_sampled(events)
         cur = prev_logp = prev_ids = None
         for level in range(w.levels):
             b = bufs[level]
@@ -346,7 +397,8 @@ def main():
             time.sleep(0.3)
         one_search()
     torch.cuda.synchronize(dev)
-    curs = [None] + [bufs[l]["nxt"].clone() for l in range(w.levels - 1)]
+    curs = [None] + [(samp_out[l][1] if w.sampling else bufs[l]["nxt"]).clone()
+                     for l in range(w.levels - 1)]
     costs = level_costs(w, dw, curs, wins)
 
     ev = [[tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
@@ -355,15 +407,19 @@ def main():
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
+    fev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(2))
+           for _ in range(args.steps)]
     t_start.record(stream)
     for s in range(args.steps):
-        one_search(ev[s])
+        one_search(ev[s], fev[s] if w.sampling else None)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     ms_total = t_start.elapsed_time(t_end)
+    if w.sampling:
+        ms_total -= sum(f[0].elapsed_time(f[1]) for f in fev)
     step_ms = [[ev[s][l][0].elapsed_time(ev[s][l][1]) for l in range(w.levels)]
                for s in range(args.steps)]
     t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
@@ -409,17 +465,31 @@ def main():
     e2e = None
     if args.e2e_steps > 0:
         host = [h.cpu().pin_memory() for h in dw.hidden]
-        outs = (torch.empty((Bq, k, w.levels), dtype=torch.int64, pin_memory=True),
-                torch.empty((Bq * k,), dtype=torch.float32, pin_memory=True),
-                torch.empty((Bq * k,), dtype=torch.int64, pin_memory=True))
-        constrained_beam_search_from_host(host, dw.weight, dw.trie, cfg, out=outs)
+        if w.sampling:
+            outs = (torch.empty((Bq, w.levels), dtype=torch.int64, pin_memory=True),
+                    torch.empty((Bq,), dtype=torch.int64, pin_memory=True))
+
+            def e2e_call():
+                dev_h = [h.to(dev, non_blocking=True) for h in host]
+                tok, node = constrained_sampling_search(dev_h, dw.weight, dw.trie, w.seed,
+                                                        temp_t)
+                outs[0].copy_(tok, non_blocking=True)
+                outs[1].copy_(node, non_blocking=True)
+        else:
+            outs = (torch.empty((Bq, k, w.levels), dtype=torch.int64, pin_memory=True),
+                    torch.empty((Bq * k,), dtype=torch.float32, pin_memory=True),
+                    torch.empty((Bq * k,), dtype=torch.int64, pin_memory=True))
+
+            def e2e_call():
+                constrained_beam_search_from_host(host, dw.weight, dw.trie, cfg, out=outs)
+        e2e_call()
         if world > 1:
             dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
         e0.record(stream)
         for _ in range(args.e2e_steps):
-            constrained_beam_search_from_host(host, dw.weight, dw.trie, cfg, out=outs)
+            e2e_call()
         e1.record(stream)
         torch.cuda.synchronize(dev)
         te = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], dtype=torch.float64, device=dev)
@@ -449,7 +519,7 @@ def main():
                 "data": "synthetic (seeded catalog, N(0,0.02) head, N(0,1) hidden states)",
                 "config": workload_cfg, "clocks": clk, "roofline": roof,
                 "cpu_baseline": cpu, "e2e": e2e,
-                "gpu_launches": args.steps * w.levels * 2}
+                "gpu_launches": args.steps * w.levels * (1 if w.sampling else 2)}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

@@ -124,6 +124,33 @@ typedef struct {
   int64_t window_n;       /* 1..256 */
 } vtnk_child_index_t;
 
+/* The _topk entry point with the depth's child index: the tcgen05 tile
+ * kernel computes the logits of the 256-token window on the tensor cores and
+ * selects the top k in its epilogue (same outputs and tie rule as
+ * vtnk_fused_linear_constrained_node_transition_topk, which it falls back to
+ * when index is NULL or the shape is not tile-able: bf16, W row-contiguous,
+ * rows >= 128, k <= 32).  cur_node NULL: every row at the root.
+ * next_node / valid_idxs may both be NULL to skip the
+ * [rows, max_branches] tables.  Called by the ops layer's
+ * fused_linear_constrained_node_transition_topk (ops/...:73-92 in the
+ * reference) when the trie depth has an index. */
+int vtnk_fused_linear_constrained_node_transition_topk_ix(
+    const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+    int64_t max_branches, int64_t k, const vtnk_child_index_t* index, int64_t* next_node,
+    int64_t* valid_idxs, float* topk_logits, int64_t* topk_idxs, void* stream);
+
+/* The _sampling entry point with the depth's child index: Gumbel-max in the
+ * tile kernel's epilogue (same noise, temperature division and first-maximum
+ * rule as vtnk_fused_linear_constrained_node_transition_sampling, its
+ * fallback).  sample_node (optional, [rows] int64) receives the sampled
+ * child's node id (-1 when none), the next level's cur_node.  next_node /
+ * valid_idxs may both be NULL. */
+int vtnk_fused_linear_constrained_node_transition_sampling_ix(
+    const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+    int64_t max_branches, uint64_t seed, const float* temperature,
+    const vtnk_child_index_t* index, int64_t* next_node, int64_t* valid_idxs, float* sample,
+    int64_t* sample_node, void* stream);
+
 /* Builds index->masks (caller memory, (node_hi - node_lo) * 32 bytes) for
  * the nodes and window described by `index` (no reference counterpart). */
 int vtnk_build_child_index(const vtnk_csr_t* csr, const vtnk_child_index_t* index,

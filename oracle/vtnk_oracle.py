@@ -175,12 +175,12 @@ def rand_uniform(seed, offsets):
     return x.astype(np.float32) * np.float32(4.6566127342e-10)
 
 
-def gumbel_noise(seed, B, max_branches):
+def gumbel_noise(seed, B, max_branches, row0=0):
     """Noise the sampling kernel adds to ``logit / T`` at (row, slot):
     ``-log(-log(u + 1e-10) + 1e-10)``, ``u = rand(seed, row * mb + slot)``
     (kernels:359-380).  fp32 arithmetic; the log is numpy's, so the last ulp
     may differ from a GPU ``logf`` -- parity tests feed the kernel's own noise."""
-    off = (np.arange(B, dtype=np.int64)[:, None] * max_branches
+    off = (np.arange(row0, row0 + B, dtype=np.int64)[:, None] * max_branches
            + np.arange(max_branches, dtype=np.int64)[None, :])
     off = ((off + 2**31) % 2**32) - 2**31  # int32 wrap, as in the Triton kernel
     u = rand_uniform(seed, off)

@@ -22,6 +22,8 @@ EXPORTS = (
     "vtnk_fused_linear_constrained_node_transition",
     "vtnk_fused_linear_constrained_node_transition_topk",
     "vtnk_fused_linear_constrained_node_transition_sampling",
+    "vtnk_fused_linear_constrained_node_transition_topk_ix",
+    "vtnk_fused_linear_constrained_node_transition_sampling_ix",
     "vtnk_gumbel_noise",
     "vtnk_build_child_index",
     "vtnk_beam_step",
@@ -82,6 +84,11 @@ def lib() -> ctypes.CDLL:
                 [POINTER(Linear), P, POINTER(Csr), I64, I64, P, P, P, P, V],
             "vtnk_fused_linear_constrained_node_transition_sampling":
                 [POINTER(Linear), P, POINTER(Csr), I64, c_uint64, P, P, P, P, V],
+            "vtnk_fused_linear_constrained_node_transition_topk_ix":
+                [POINTER(Linear), P, POINTER(Csr), I64, I64, POINTER(ChildIndex), P, P, P, P, V],
+            "vtnk_fused_linear_constrained_node_transition_sampling_ix":
+                [POINTER(Linear), P, POINTER(Csr), I64, c_uint64, P, POINTER(ChildIndex), P, P,
+                 P, P, V],
             "vtnk_gumbel_noise": [c_uint64, I64, I64, P, V],
             "vtnk_build_child_index": [POINTER(Csr), POINTER(ChildIndex), V],
             "vtnk_beam_step": [POINTER(Linear), P, POINTER(Csr), I64, I64, POINTER(ChildIndex),

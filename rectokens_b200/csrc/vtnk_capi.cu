@@ -110,12 +110,13 @@ SearchLayout search_layout(const vtnk_search_t* s) {
   return L;
 }
 
-// One fused level: tcgen05 tile kernel when the shape allows, else rows kernel.
-int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
-                   int64_t mb, int64_t n_cand, const vtnk_child_index_t* index,
-                   int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
-                   cudaStream_t s) {
-  if (lin->rows == 0) return VTNK_OK;
+// The tcgen05 tile kernel for one level when the shape allows it;
+// VTNK_ERR_UNSUPPORTED (nothing launched) otherwise.  `sample` selects
+// Gumbel-max sampling (n_cand 1) instead of top-n + log-sum-exp.
+int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr, int64_t mb,
+            int64_t n_cand, const vtnk_child_index_t* index, int64_t* cand_tok,
+            float* cand_logit, int64_t* cand_node, float* row_lse, int sample, uint64_t seed,
+            const float* temperature, float* sample_f, cudaStream_t s) {
   if (tc_enabled() && index && index->masks && lin->dtype == VTNK_BF16 && lin->b_stride_k == 1 &&
       lin->rows >= 128) {
     TcArgs t{};
@@ -140,9 +141,24 @@ int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk
     t.cand_logit = cand_logit;
     t.cand_node = cand_node;
     t.row_lse = row_lse;
-    const int rc = launch_beam_step_tc(t, s);
-    if (rc != VTNK_ERR_UNSUPPORTED) return rc;
+    t.sample = sample;
+    t.seed = seed;
+    t.temperature = temperature;
+    t.sample_f = sample_f;
+    return launch_beam_step_tc(t, s);
   }
+  return VTNK_ERR_UNSUPPORTED;
+}
+
+// One fused level: tcgen05 tile kernel when the shape allows, else rows kernel.
+int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+                   int64_t mb, int64_t n_cand, const vtnk_child_index_t* index,
+                   int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
+                   cudaStream_t s) {
+  if (lin->rows == 0) return VTNK_OK;
+  const int rc = tc_step(lin, cur_node, csr, mb, n_cand, index, cand_tok, cand_logit, cand_node,
+                         row_lse, 0, 0, nullptr, nullptr, s);
+  if (rc != VTNK_ERR_UNSUPPORTED) return rc;
   RowsArgs p = rows_from(lin, cur_node, csr, mb);
   p.k = static_cast<int>(n_cand);
   p.buf_cap = static_cast<int>(mb > 0 ? mb : 1);
@@ -233,6 +249,66 @@ int vtnk_fused_linear_constrained_node_transition_sampling(
   p.valid_idxs = valid_idxs;
   p.sample = sample;
   return launch_rows(p, MODE_SAMPLE, lin->dtype, as_stream(stream));
+}
+
+int vtnk_fused_linear_constrained_node_transition_topk_ix(
+    const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+    int64_t max_branches, int64_t k, const vtnk_child_index_t* index, int64_t* next_node,
+    int64_t* valid_idxs, float* topk_logits, int64_t* topk_idxs, void* stream) {
+  int rc = check_step(lin, csr, max_branches);
+  if (rc) return rc;
+  VTNK_REQUIRE(k >= 1 && k <= max_branches, "k (%lld) must be in [1, max_branches=%lld]",
+               (long long)k, (long long)max_branches);
+  VTNK_REQUIRE(lin->rows == 0 || (topk_logits && topk_idxs), "NULL pointer");
+  VTNK_REQUIRE((next_node == nullptr) == (valid_idxs == nullptr),
+               "next_node and valid_idxs are both given or both NULL");
+  if (lin->rows == 0) return VTNK_OK;
+  cudaStream_t s = as_stream(stream);
+  rc = tc_step(lin, cur_node, csr, max_branches, k, index, topk_idxs, topk_logits, nullptr,
+               nullptr, 0, 0, nullptr, nullptr, s);
+  if (rc == VTNK_ERR_UNSUPPORTED) {
+    RowsArgs p = rows_from(lin, cur_node, csr, max_branches);
+    p.k = static_cast<int>(k);
+    p.buf_cap = static_cast<int>(max_branches);
+    p.next_node = next_node;
+    p.valid_idxs = valid_idxs;
+    p.out_logit = topk_logits;
+    p.out_tok = topk_idxs;
+    return launch_rows(p, MODE_TOPK, lin->dtype, s);
+  }
+  if (rc || !next_node) return rc;
+  return launch_tables(lin->rows, cur_node, make_csr(*csr), max_branches, next_node, valid_idxs,
+                       s);
+}
+
+int vtnk_fused_linear_constrained_node_transition_sampling_ix(
+    const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
+    int64_t max_branches, uint64_t seed, const float* temperature,
+    const vtnk_child_index_t* index, int64_t* next_node, int64_t* valid_idxs, float* sample,
+    int64_t* sample_node, void* stream) {
+  int rc = check_step(lin, csr, max_branches);
+  if (rc) return rc;
+  VTNK_REQUIRE(lin->rows == 0 || sample, "NULL pointer");
+  VTNK_REQUIRE((next_node == nullptr) == (valid_idxs == nullptr),
+               "next_node and valid_idxs are both given or both NULL");
+  if (lin->rows == 0) return VTNK_OK;
+  cudaStream_t s = as_stream(stream);
+  rc = tc_step(lin, cur_node, csr, max_branches, 1, index, nullptr, nullptr, sample_node, nullptr,
+               1, seed, temperature, sample, s);
+  if (rc == VTNK_ERR_UNSUPPORTED) {
+    RowsArgs p = rows_from(lin, cur_node, csr, max_branches);
+    p.seed = seed;
+    p.temperature = temperature;
+    p.buf_cap = static_cast<int>(max_branches > 0 ? max_branches : 1);
+    p.next_node = next_node;
+    p.valid_idxs = valid_idxs;
+    p.sample = sample;
+    p.out_node = sample_node;
+    return launch_rows(p, MODE_SAMPLE, lin->dtype, s);
+  }
+  if (rc || !next_node) return rc;
+  return launch_tables(lin->rows, cur_node, make_csr(*csr), max_branches, next_node, valid_idxs,
+                       s);
 }
 
 int vtnk_gumbel_noise(uint64_t seed, int64_t rows, int64_t max_branches, float* out,

@@ -29,7 +29,7 @@ struct RowsArgs {
   int64_t* valid_idxs;
   float* out_logit;         // MODE_TOPK topk_logits / MODE_BEAM cand_logit [rows, k]
   int64_t* out_tok;         // MODE_TOPK topk_idxs / MODE_BEAM cand_tok
-  int64_t* out_node;        // MODE_BEAM cand_node
+  int64_t* out_node;        // MODE_BEAM cand_node / MODE_SAMPLE sampled child (optional)
   float* out_lse;           // MODE_BEAM [rows]
   float* sample;            // MODE_SAMPLE [rows]
 };
@@ -67,8 +67,12 @@ struct TcArgs {
   int n_cand;
   int64_t* cand_tok;
   float* cand_logit;
-  int64_t* cand_node;
-  float* row_lse;
+  int64_t* cand_node;        // optional
+  float* row_lse;            // optional
+  int sample;                // 1: Gumbel-max sampling (n_cand == 1)
+  uint64_t seed;
+  const float* temperature;  // device scalar or nullptr (1)
+  float* sample_f;           // optional: sampled token id as float, -1 when none
 };
 
 int launch_rows(const RowsArgs& p, int mode, int dtype, cudaStream_t s);
@@ -79,6 +83,8 @@ int launch_merge(const MergeArgs& p, cudaStream_t s);
 int launch_synth(uint64_t key, int64_t e0, int64_t count, const void* table, int dtype, void* out,
                  cudaStream_t s);
 int launch_gumbel(uint64_t seed, int64_t rows, int64_t mb, float* out, cudaStream_t s);
+int launch_tables(int64_t rows, const int64_t* cur_node, const Csr& csr, int64_t mb,
+                  int64_t* next_node, int64_t* valid_idxs, cudaStream_t s);
 
 // Returns VTNK_ERR_UNSUPPORTED (without launching) when the shape does not
 // fit the tile kernel; the caller then uses the row kernel.

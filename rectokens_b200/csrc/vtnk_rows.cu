@@ -42,7 +42,7 @@ rows_kernel(const RowsArgs p) {
     int count;
     node_children(p.csr, cur, p.mb, start, count);
 
-    if (MODE != MODE_BEAM) {  // branch tables [rows, mb], -1 padded
+    if (MODE != MODE_BEAM && p.next_node) {  // branch tables [rows, mb], -1 padded
       int64_t* vi = p.valid_idxs + row * p.mb;
       int64_t* nn = p.next_node + row * p.mb;
       for (int j = lane; j < p.mb; j += 32) {
@@ -167,10 +167,11 @@ rows_kernel(const RowsArgs p) {
         }
       }
       warp_argmax(bv, bj);
-      if (lane == 0)
-        p.sample[row] = (bj != INT_MAX && bv > -INFINITY)
-                            ? static_cast<float>(__ldg(cols + start + bj))
-                            : -1.f;
+      if (lane == 0) {
+        const bool ok = bj != INT_MAX && bv > -INFINITY;
+        p.sample[row] = ok ? static_cast<float>(__ldg(cols + start + bj)) : -1.f;
+        if (p.out_node) p.out_node[row] = ok ? __ldg(vals + start + bj) : -1;
+      }
     }
     __syncwarp();
   }
@@ -526,6 +527,25 @@ __global__ void synth_kernel(uint64_t key, int64_t e0, int64_t count, const T* _
   }
 }
 
+// Branch tables alone: valid_idxs / next_node [rows, mb], -1 padded (warp per row).
+__global__ void __launch_bounds__(kWarps * 32)
+tables_kernel(int64_t rows, const int64_t* __restrict__ cur_node, const Csr csr, int64_t mb,
+              int64_t* __restrict__ next_node, int64_t* __restrict__ valid_idxs) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp; row < rows;
+       row += static_cast<int64_t>(gridDim.x) * kWarps) {
+    int64_t start;
+    int count;
+    node_children(csr, cur_node ? __ldg(cur_node + row) : 0, mb, start, count);
+    for (int j = lane; j < mb; j += 32) {
+      const bool ok = j < count;
+      valid_idxs[row * mb + j] = ok ? __ldg(csr.cols + start + j) : -1;
+      next_node[row * mb + j] = ok ? __ldg(csr.vals + start + j) : -1;
+    }
+  }
+}
+
 __global__ void gumbel_kernel(uint64_t seed, int64_t rows, int64_t mb, float* out) {
   const int64_t n = rows * mb;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
@@ -678,6 +698,14 @@ int launch_synth(uint64_t key, int64_t e0, int64_t count, const void* table, int
     synth_kernel<float><<<grid, 256, 0, s>>>(key, e0, count, static_cast<const float*>(table),
                                              static_cast<float*>(out));
   return cuda_status(cudaGetLastError(), "synth_kernel launch");
+}
+
+int launch_tables(int64_t rows, const int64_t* cur_node, const Csr& csr, int64_t mb,
+                  int64_t* next_node, int64_t* valid_idxs, cudaStream_t s) {
+  if (rows == 0 || mb == 0) return VTNK_OK;
+  tables_kernel<<<grid_for(rows, kWarps), kWarps * 32, 0, s>>>(rows, cur_node, csr, mb, next_node,
+                                                               valid_idxs);
+  return cuda_status(cudaGetLastError(), "tables_kernel launch");
 }
 
 int launch_gumbel(uint64_t seed, int64_t rows, int64_t mb, float* out, cudaStream_t s) {

@@ -109,6 +109,9 @@ struct Params {
   float* cand_logit;
   int64_t* cand_node;
   float* row_lse;
+  uint64_t seed;             // sampling: Philox key
+  const float* temperature;  // sampling: device scalar (nullptr: 1)
+  float* sample_f;           // sampling: token id as float, -1 when none (optional)
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -149,7 +152,9 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatil
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
   for (uint32_t i = 1;; ++i) {
+#ifndef VTNK_TC_NOSLEEP
     if (ns) __nanosleep(ns);  // back off so a waiting role does not steal issue slots
+#endif
     if (mbar_try_wait(b, parity)) return true;
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
@@ -200,7 +205,9 @@ __device__ __forceinline__ bool wait_phase_cluster(uint64_t* b, uint32_t parity,
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
   for (uint32_t i = 1;; ++i) {
+#ifndef VTNK_TC_NOSLEEP
     if (ns) __nanosleep(ns);
+#endif
     if (mbar_try_wait_cluster(b, parity)) return true;
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
@@ -222,6 +229,26 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(su32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
       : "memory");
+}
+// Same, with an L2 eviction-priority policy (createpolicy).
+__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const CUtensorMap* map,
+                                                      uint32_t leader_bar, int x, int y,
+                                                      uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
 }
 
 // Warp-level wait for the epilogue: one lane polls, with a growing sleep
@@ -429,9 +456,11 @@ __device__ __forceinline__ void load_chunk(uint32_t taddr, int chunk, const uint
 // Exact per-row path for a row whose node is outside the index or whose
 // children are not a clean sorted in-window set (slow, never taken for a
 // sorted catalog trie queried at the right depth).
+// With `sample`, the value pushed for slot j is the Gumbel score
+// logit / temp + g(row * mb + j) and no log-sum-exp is formed.
 template <int NC>
 __device__ void row_scalar(const Params& p, int64_t row, int64_t start, int count, TopN<NC>& t,
-                           float& lse) {
+                           float& lse, bool sample, float temp) {
   const __nv_bfloat16* ar = p.a + row * p.a_stride;
   float m = -INFINITY, s = 0.f;
   for (int j = 0; j < count; ++j) {
@@ -448,12 +477,16 @@ __device__ void row_scalar(const Params& p, int64_t row, int64_t start, int coun
     } else {
       s += __expf(acc - m);
     }
-    t.push(acc, j);  // slot index; mapped to token / node by the caller
+    if (sample)
+      t.push(acc / temp + gumbel_at(p.seed, static_cast<uint32_t>(row * p.mb + j)), j);
+    else
+      t.push(acc, j);  // slot index; mapped to token / node by the caller
   }
   lse = (m > -INFINITY) ? m + __logf(s) : -INFINITY;
 }
 
-template <int NC>
+// SAMPLE: Gumbel-max sampling (NC == 1) instead of top-n + log-sum-exp.
+template <int NC, bool SAMPLE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                  const Params p) {
@@ -509,6 +542,10 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+#ifdef VTNK_TC_L2HINTS
+      const uint64_t pol_a = policy_evict_first();  // hidden states: read once
+      const uint64_t pol_w = policy_evict_last();   // head window: read by every tile
+#endif
       uint32_t armed[STAGES] = {};
       long long prof_wait = 0;
       int stage = 0;
@@ -525,10 +562,25 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
           PROF_ACC(prof_wait, t_w);
           uint8_t* st = S.ring[stage];
+#ifdef VTNK_TC_EXPERIMENT_NOW
+          // tuning experiment only (outputs meaningless): A copies alone
+          if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * A_BYTES);
+#else
           if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * STAGE_BYTES);
+#endif
           const uint32_t lbar = map_to_rank(&S.full[stage], 0);
+#ifdef VTNK_TC_L2HINTS
+          tma_load_2d_pair_hint(st, &tmA, lbar, kb * BK, arow, pol_a);
+#else
           tma_load_2d_pair(st, &tmA, lbar, kb * BK, arow);
+#endif
+#ifndef VTNK_TC_EXPERIMENT_NOW
+#ifdef VTNK_TC_L2HINTS
+          tma_load_2d_pair_hint(st + A_BYTES, &tmW, lbar, kb * BK, wrow, pol_w);
+#else
           tma_load_2d_pair(st + A_BYTES, &tmW, lbar, kb * BK, wrow);
+#endif
+#endif
           ++armed[stage];
           if (++stage == STAGES) {
             stage = 0;
@@ -632,6 +684,13 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tc_fence_after();
       PROF_ACC(pe_wait, t_wt);
       PROF_T0(t_tm);
+#ifdef VTNK_TC_EXPERIMENT_NOEPI
+      // tuning experiment only (no outputs written): release the accumulator at once
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);
+      continue;
+#endif
 
       TopN<NC> top;
       top.init();
@@ -639,73 +698,113 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BN;
       const bool has_bias = p.bias != nullptr;
       const int c0 = half * (BN / 64);  // this warp's first 32-column chunk
-      // Pass 1 over the accumulator: online log-sum-exp, and the maxima of G
-      // column groups (column j of the half in group j % G).  The NC-th largest
-      // group maximum is a lower bound of the NC-th largest value (the NC
-      // largest group maxima are NC distinct entries), so pass 2 only inserts
-      // values at or above it.
-      constexpr int G = NC <= VTNK_TC_GROUPS ? VTNK_TC_GROUPS : 32;
-      float gm[G];
+      const float temp = (SAMPLE && p.temperature) ? __ldg(p.temperature) : 1.f;
+      if constexpr (SAMPLE) {
+        // Gumbel-max over this half's children: score = logit / T + g, with
+        // g drawn at the reference's flat offset row * mb + slot (int32 wrap).
+        // Each lane visits its children in slot order and keeps the first
+        // maximum; the lower half wins ties in the hand-off below.
+        int pre_h = 0;  // children in the chunks before this warp's first
 #pragma unroll
-      for (int g = 0; g < G; ++g) gm[g] = -INFINITY;
-      float cmax[BN / 64];
-#pragma unroll
-      for (int ci = 0; ci < BN / 64; ++ci) {
-        const int chunk = c0 + ci;
-        float x[32];
-        load_chunk(taddr, chunk, m, has_bias, S.bias, x);
-        const float cm = tree_max<32>(x);
-        cmax[ci] = cm;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) gm[i % G] = fmaxf(gm[i % G], x[i]);
-        const float nm = fmaxf(mx, cm);
-        sum *= (nm == mx) ? 1.f : __expf(mx - nm);
-        mx = nm;
-        float e[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) e[i] = (x[i] > -INFINITY) ? __expf(x[i] - mx) : 0.f;
-#pragma unroll
-        for (int w = 16; w >= 1; w >>= 1)
-#pragma unroll
-          for (int i = 0; i < w; ++i) e[i] += e[i + w];
-        sum += e[0];
-      }
-      const float lb = nth_largest<G, NC>(gm);
-      // Pass 2: top-n in column order over the values >= lb.  Each lane
-      // inserts only its values above its current n-th best; the warp loops
-      // max-over-lanes(candidates) times.  Values are read back from shared
-      // memory ([col][lane]: conflict-free for any per-lane column).
-      float* sx = &S.chunk_x[warp - 2][0][0];
+        for (int i = 0; i < BN / 32; ++i) pre_h += (i < c0) ? __popc(m[i]) : 0;
+        float* sx = &S.chunk_x[warp - 2][0][0];
+        const uint32_t off0 = static_cast<uint32_t>(row * p.mb);
 #pragma unroll 1
-      for (int ci = 0; ci < BN / 64; ++ci) {
-        if (!__any_sync(0xffffffffu, cmax[ci] >= lb && cmax[ci] > -INFINITY)) continue;
-        const int chunk = c0 + ci;
-        float x[32];
-        load_chunk(taddr, chunk, m, has_bias, S.bias, x);
-        const float thr = top.v[NC - 1];
-        uint32_t pend = 0;
-        __syncwarp();
+        for (int ci = 0; ci < BN / 64; ++ci) {
+          const int chunk = c0 + ci;
+          uint32_t mw = 0;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          pend |= (x[i] > thr && x[i] >= lb) ? (1u << i) : 0u;
-          sx[i * 32 + lane] = x[i];
+          for (int i = 0; i < BN / 32; ++i) mw = (i == chunk) ? m[i] : mw;
+          if (spill) mw = 0u;  // recomputed exactly below
+          if (__any_sync(0xffffffffu, mw != 0u)) {
+            float x[32];
+            load_chunk(taddr, chunk, m, has_bias, S.bias, x);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) sx[i * 32 + lane] = x[i];
+            __syncwarp();
+            uint32_t pend = mw;
+            while (__any_sync(0xffffffffu, pend != 0u)) {
+              if (pend) {
+                const int i = __ffs(pend) - 1;
+                pend &= pend - 1;
+                const int slot = pre_h + __popc(mw & ((1u << i) - 1u));
+                const float g = gumbel_at(p.seed, off0 + static_cast<uint32_t>(slot));
+                top.push(sx[i * 32 + lane] / temp + g, chunk * 32 + i);
+              }
+            }
+          }
+          pre_h += __popc(mw);
         }
-        __syncwarp();
+      } else {
+        // Pass 1 over the accumulator: online log-sum-exp, and the maxima of G
+        // column groups (column j of the half in group j % G).  The NC-th largest
+        // group maximum is a lower bound of the NC-th largest value (the NC
+        // largest group maxima are NC distinct entries), so pass 2 only inserts
+        // values at or above it.
+        constexpr int G = NC <= VTNK_TC_GROUPS ? VTNK_TC_GROUPS : 32;
+        float gm[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) gm[g] = -INFINITY;
+        float cmax[BN / 64];
+#pragma unroll
+        for (int ci = 0; ci < BN / 64; ++ci) {
+          const int chunk = c0 + ci;
+          float x[32];
+          load_chunk(taddr, chunk, m, has_bias, S.bias, x);
+          const float cm = tree_max<32>(x);
+          cmax[ci] = cm;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) gm[i % G] = fmaxf(gm[i % G], x[i]);
+          const float nm = fmaxf(mx, cm);
+          sum *= (nm == mx) ? 1.f : __expf(mx - nm);
+          mx = nm;
+          float e[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) e[i] = (x[i] > -INFINITY) ? __expf(x[i] - mx) : 0.f;
+#pragma unroll
+          for (int w = 16; w >= 1; w >>= 1)
+#pragma unroll
+            for (int i = 0; i < w; ++i) e[i] += e[i + w];
+          sum += e[0];
+        }
+        const float lb = nth_largest<G, NC>(gm);
+        // Pass 2: top-n in column order over the values >= lb.  Each lane
+        // inserts only its values above its current n-th best; the warp loops
+        // max-over-lanes(candidates) times.  Values are read back from shared
+        // memory ([col][lane]: conflict-free for any per-lane column).
+        float* sx = &S.chunk_x[warp - 2][0][0];
+#pragma unroll 1
+        for (int ci = 0; ci < BN / 64; ++ci) {
+          if (!__any_sync(0xffffffffu, cmax[ci] >= lb && cmax[ci] > -INFINITY)) continue;
+          const int chunk = c0 + ci;
+          float x[32];
+          load_chunk(taddr, chunk, m, has_bias, S.bias, x);
+          const float thr = top.v[NC - 1];
+          uint32_t pend = 0;
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            pend |= (x[i] > thr && x[i] >= lb) ? (1u << i) : 0u;
+            sx[i * 32 + lane] = x[i];
+          }
+          __syncwarp();
 #ifdef VTNK_TC_EXPERIMENT_NOSELECT
-        pend = 0u;  // tuning experiment only: measures the pipeline without top-n work
+          pend = 0u;  // tuning experiment only: measures the pipeline without top-n work
 #endif
-        // software-pipelined: the next candidate's shared-memory read overlaps
-        // the current insert
-        int inext = pend ? __ffs(pend) - 1 : -1;
-        pend &= pend - 1;
-        float ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
-        while (__any_sync(0xffffffffu, inext >= 0)) {
-          const float y = ynext;
-          const int col = chunk * 32 + inext;
-          inext = pend ? __ffs(pend) - 1 : -1;
+          // software-pipelined: the next candidate's shared-memory read overlaps
+          // the current insert
+          int inext = pend ? __ffs(pend) - 1 : -1;
           pend &= pend - 1;
-          ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
-          top.insert(y, col);  // no-op for -inf / values no longer above the n-th best
+          float ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
+          while (__any_sync(0xffffffffu, inext >= 0)) {
+            const float y = ynext;
+            const int col = chunk * 32 + inext;
+            inext = pend ? __ffs(pend) - 1 : -1;
+            pend &= pend - 1;
+            ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
+            top.insert(y, col);  // no-op for -inf / values no longer above the n-th best
+          }
         }
       }
       __syncwarp();
@@ -763,7 +862,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       bool by_slot = false;
       if (spill && live) {  // exact scalar recompute of this row
         top.init();
-        row_scalar<NC>(p, row, start, count, top, lse);
+        row_scalar<NC>(p, row, start, count, top, lse, SAMPLE, temp);
         by_slot = true;
       }
       if (live) {
@@ -774,9 +873,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           pre[i] = acc;
           acc += __popc(m[i]);
         }
-        int64_t* ot = p.cand_tok + row * p.n_cand;
-        float* ol = p.cand_logit + row * p.n_cand;
-        int64_t* on = p.cand_node + row * p.n_cand;
+        const int64_t o = row * p.n_cand;
 #pragma unroll
         for (int j = 0; j < NC; ++j) {
           if (j >= p.n_cand) break;
@@ -803,11 +900,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             node = __ldg(p.csr.vals + start + slot);
             lv = top.v[j];
           }
-          ot[j] = tok;
-          ol[j] = lv;
-          on[j] = node;
+          if (p.cand_tok) p.cand_tok[o + j] = tok;
+          if (p.cand_logit) p.cand_logit[o + j] = lv;  // sampling: the winning score
+          if (p.cand_node) p.cand_node[o + j] = node;
+          if (SAMPLE && p.sample_f) p.sample_f[row] = tok >= 0 ? static_cast<float>(tok) : -1.f;
         }
-        p.row_lse[row] = lse;
+        if (p.row_lse) p.row_lse[row] = lse;
       }
       PROF_ACC(pe_out, t_out);
     }
@@ -909,9 +1007,9 @@ int sm_count() {
   return n;
 }
 
-template <int NC>
+template <int NC, bool SAMPLE = false>
 int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, cudaStream_t s) {
-  auto k = beam_step_kernel<NC>;
+  auto k = beam_step_kernel<NC, SAMPLE>;
   cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        static_cast<int>(SMEM_BYTES));
   const int64_t pairs = (p.rows + PAIR_M - 1) / PAIR_M;  // one 256-row tile per pair step
@@ -963,12 +1061,16 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.cand_logit = t.cand_logit;
   p.cand_node = t.cand_node;
   p.row_lse = t.row_lse;
+  p.seed = t.seed;
+  p.temperature = t.temperature;
+  p.sample_f = t.sample_f;
   CUtensorMap ma, mw;
   if (!make_map(&ma, t.a, t.H, t.rows, t.a_stride * 2, BK, BM) ||
       !make_map(&mw, t.w, t.H, t.n_vocab, t.w_stride * 2, BK, BN / 2)) {
     set_error("cuTensorMapEncodeTiled failed");
     return VTNK_ERR_CUDA;
   }
+  if (t.sample) return t.n_cand == 1 ? launch_nc<1, true>(ma, mw, p, s) : VTNK_ERR_UNSUPPORTED;
   switch (t.n_cand) {  // exact widths for the common beam sizes
     case 1: return launch_nc<1>(ma, mw, p, s);
     case 5: return launch_nc<5>(ma, mw, p, s);

@@ -296,3 +296,52 @@ def constrained_beam_search_from_host(
     out[2].copy_(cur, non_blocking=True)
     main.synchronize()
     return BeamSearchResult(*out)
+
+
+# ------------------------------------------------------------------ sampled search
+def sample_step(a: Tensor, weight: Tensor, trie: CompactCSRTrie, step: int,
+                cur_node: Tensor | None, seed: int, temperature: Tensor,
+                bias: Tensor | None = None, index="auto", out=None):
+    """One Gumbel-max sampling level (the reference's ``_sampling`` op,
+    kernels:562-783, without its ``[rows, mb]`` tables): ``(sample, node)``
+    with ``sample`` the sampled token id as float32 (-1.0 when a row has no
+    child) and ``node`` the sampled child's node id (the next level's
+    ``cur_node``).  ``temperature``: CUDA fp32 scalar tensor."""
+    dev = a.device
+    R = a.shape[0]
+    mb = trie.layer_max_branches[step]
+    if isinstance(index, str):
+        index = child_index(trie, step)
+    if out is None:
+        out = (torch.empty((R,), dtype=torch.float32, device=dev),
+               torch.empty((R,), dtype=torch.int64, device=dev))
+    lin = L.linear_struct(a, weight.T, bias)
+    csr = L.csr_struct(trie.row_ptrs, trie.stacked_cols_vals)
+    L.check(L.lib().vtnk_fused_linear_constrained_node_transition_sampling_ix(
+        lin, L.ptr(cur_node), csr, mb, seed & 0xFFFFFFFFFFFFFFFF, temperature.data_ptr(), index,
+        None, None, out[0].data_ptr(), out[1].data_ptr(), L.stream_of(dev)))
+    return out
+
+
+def constrained_sampling_search(hidden: Sequence[Tensor], weight: Tensor, trie: CompactCSRTrie,
+                                seed: int, temperature: float | Tensor,
+                                bias: Tensor | None = None):
+    """``L = len(hidden)`` levels of trie-constrained Gumbel-max sampling, one
+    sample per row (``hidden[l]``: ``(B, H)`` CUDA tensors, row ``b`` of every
+    level is sequence ``b``).  Every level draws with ``seed`` at the
+    reference's offsets ``row * mb + slot``.  Returns ``(tokens (B, L) int64,
+    node (B,) int64)``; a row that reaches a node without children gets -1."""
+    dev = weight.device
+    if not isinstance(temperature, Tensor):
+        temperature = torch.tensor([float(temperature)], dtype=torch.float32, device=dev)
+    B = hidden[0].shape[0]
+    samples = torch.empty((len(hidden), B), dtype=torch.float32, device=dev)
+    node = torch.empty((B,), dtype=torch.int64, device=dev)
+    nodes = [torch.empty((B,), dtype=torch.int64, device=dev) for _ in range(2)]
+    cur = None
+    for l, h in enumerate(hidden):
+        nxt = nodes[l & 1]
+        sample_step(h, weight, trie, l, cur, seed, temperature, bias, out=(samples[l], nxt))
+        cur = nxt
+    node.copy_(cur)
+    return samples.t().to(torch.int64), node

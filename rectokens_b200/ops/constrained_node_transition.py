@@ -15,11 +15,28 @@ import torch
 from rectokens_b200.ops._vtnk_ops import (
     _constrained_node_transition_op,
     _fused_linear_constrained_node_transition_op,
+    _fused_linear_constrained_node_transition_sampling_ix_op,
     _fused_linear_constrained_node_transition_sampling_op,
+    _fused_linear_constrained_node_transition_topk_ix_op,
     _fused_linear_constrained_node_transition_topk_op,
     default_seed,
 )
 from rectokens_b200.schemas.state import ConstraintState
+
+
+def _tile_index(a: torch.Tensor, constraint_state: ConstraintState):
+    """``(masks, node_lo, node_hi, window_lo, window_n)`` of the step's depth
+    when the tile kernel can serve the call (bf16 CUDA operands, a child
+    index for the depth), else None."""
+    if a.dtype != torch.bfloat16 or a.device.type != "cuda" or a.shape[0] < 128:
+        return None
+    from rectokens_b200.decoding.beam_search import child_index, child_index_masks
+
+    trie, step = constraint_state.trie, constraint_state.step
+    ci = child_index(trie, step)
+    if ci is None:
+        return None
+    return (child_index_masks(trie, step), ci.node_lo, ci.node_hi, ci.window_lo, ci.window_n)
 
 
 def fused_linear_constrained_node_transition(
@@ -64,6 +81,12 @@ def fused_linear_constrained_node_transition_sampling(
         temperature = 1.0
     if not isinstance(temperature, torch.Tensor):
         temperature = torch.tensor([float(temperature)], dtype=torch.float32, device=a.device)
+    ix = _tile_index(a, constraint_state)
+    if ix is not None:
+        return _fused_linear_constrained_node_transition_sampling_ix_op(
+            a, b, bias_val, constraint_state.cur_node, constraint_state.trie.row_ptrs,
+            constraint_state.trie.stacked_cols_vals, *ix, max_branches, bias is not None,
+            int(rng_seed), temperature)
     return _fused_linear_constrained_node_transition_sampling_op(
         a, b, bias_val, constraint_state.cur_node, constraint_state.trie.row_ptrs,
         constraint_state.trie.stacked_cols_vals, max_branches, bias is not None,
@@ -85,6 +108,11 @@ def fused_linear_constrained_node_transition_topk(
     """
     bias_val = bias if bias is not None else a.new_empty(0)
     max_branches = constraint_state.trie.layer_max_branches[constraint_state.step]
+    ix = _tile_index(a, constraint_state)
+    if ix is not None:
+        return _fused_linear_constrained_node_transition_topk_ix_op(
+            a, b, bias_val, constraint_state.cur_node, constraint_state.trie.row_ptrs,
+            constraint_state.trie.stacked_cols_vals, *ix, max_branches, bias is not None, k)
     return _fused_linear_constrained_node_transition_topk_op(
         a, b, bias_val, constraint_state.cur_node, constraint_state.trie.row_ptrs,
         constraint_state.trie.stacked_cols_vals, max_branches, bias is not None, k)
