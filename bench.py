@@ -246,9 +246,6 @@ def main():
         "global_batch": w.batch, "beams": w.beams, "topk": w.topk, "levels": w.levels,
         "hidden": w.hidden, "rows_per_search": S.search_rows(w),
         "parallelism": f"dp{args.gpus}" if args.gpus > 1 else "single",
-        "l2": ("hidden states of a level (29 MB) fit in L2: a 256 MB buffer is written "
-               "between timed searches" if w.sampling else
-               "inputs larger than L2 (hidden states >= 0.47 GB per level), no flush"),
     }
 
     if args.impl == "reference":
@@ -335,9 +332,10 @@ def main():
     temp_t = torch.tensor([w.temperature], dtype=torch.float32, device=dev)
     samp_out = [(torch.empty((R,), dtype=torch.float32, device=dev),
                  torch.empty((R,), dtype=torch.int64, device=dev)) for R in rows_l]
-    flush = torch.empty((256 << 20,), dtype=torch.uint8, device=dev) if w.sampling else None
+    flush = None
 
-    def one_sampled(events=None):
+    def one_sampled(events=None, sp=None):
+        sp = sptr if sp is None else sp
         cur = None
         for level in range(w.levels):
             smp, nd = samp_out[level]
@@ -345,41 +343,46 @@ def main():
                 events[level][0].record(stream)
             L.check(lib.vtnk_fused_linear_constrained_node_transition_sampling_ix(
                 lins[level], L.ptr(cur), csr, dw.trie.layer_max_branches[level], w.seed,
-                temp_t.data_ptr(), idxs[level], None, None, smp.data_ptr(), nd.data_ptr(), sptr))
+                temp_t.data_ptr(), idxs[level], None, None, smp.data_ptr(), nd.data_ptr(), sp))
             if events is not None:
                 events[level][1].record(stream)
                 events[level][2].record(stream)
             cur = nd
         return cur
 
-    def one_search(events=None, flush_ev=None):
+    def step_launch(level, cur, sp):
+        b = bufs[level]
+        L.check(lib.vtnk_beam_step(lins[level], L.ptr(cur), csr,
+                                   dw.trie.layer_max_branches[level], w.topk,
+                                   idxs[level], b["tok"].data_ptr(),
+                                   b["logit"].data_ptr(), b["node"].data_ptr(),
+                                   b["lse"].data_ptr(), sp))
+
+    def merge_launch(level, prev_logp, prev_ids, sp):
+        b = bufs[level]
+        L.check(lib.vtnk_beam_merge(level, Bq, k, w.topk, b["tok"].data_ptr(),
+                                    b["logit"].data_ptr(), b["node"].data_ptr(),
+                                    b["lse"].data_ptr(), L.ptr(prev_logp), L.ptr(prev_ids),
+                                    b["ids"].data_ptr(), b["logp"].data_ptr(),
+                                    b["nxt"].data_ptr(), b["parent"].data_ptr(), sp))
+
+    def one_search(events=None, sp=None, gather=True):
+        sp = sptr if sp is None else sp
         if w.sampling:
-            if flush_ev is not None:  # L2 flush between timed searches, timed and subtracted
-                flush_ev[0].record(stream)
-                flush.fill_(1)
-                flush_ev[1].record(stream)
-            return one_sampled(events)
+            return one_sampled(events, sp)
         cur = prev_logp = prev_ids = None
         for level in range(w.levels):
             b = bufs[level]
             if events is not None:
                 events[level][0].record(stream)
-            L.check(lib.vtnk_beam_step(lins[level], L.ptr(cur), csr,
-                                       dw.trie.layer_max_branches[level], w.topk,
-                                       idxs[level], b["tok"].data_ptr(),
-                                       b["logit"].data_ptr(), b["node"].data_ptr(),
-                                       b["lse"].data_ptr(), sptr))
+            step_launch(level, cur, sp)
             if events is not None:
                 events[level][1].record(stream)
-            L.check(lib.vtnk_beam_merge(level, Bq, k, w.topk, b["tok"].data_ptr(),
-                                        b["logit"].data_ptr(), b["node"].data_ptr(),
-                                        b["lse"].data_ptr(), L.ptr(prev_logp), L.ptr(prev_ids),
-                                        b["ids"].data_ptr(), b["logp"].data_ptr(),
-                                        b["nxt"].data_ptr(), b["parent"].data_ptr(), sptr))
+            merge_launch(level, prev_logp, prev_ids, sp)
             if events is not None:
                 events[level][2].record(stream)
             cur, prev_logp, prev_ids = b["nxt"], b["logp"], b["ids"]
-        if world > 1:
+        if world > 1 and gather:
             gather_results(prev_ids, prev_logp, cur, out=gather_out)
         return cur
 
@@ -401,8 +404,58 @@ def main():
                      for l in range(w.levels - 1)]
     costs = level_costs(w, dw, curs, wins)
 
-    ev = [[tuple(torch.cuda.Event(enable_timing=True) for _ in range(3))
-           for _ in range(w.levels)] for _ in range(args.steps)]
+    # One search (every level's step and merge) captured as a CUDA graph and
+    # replayed: the timed loop measures the device, not the host's launch
+    # rate.  Per-level kernel times come from graphs of each launch alone.
+    # Workloads whose inputs fit in L2 get a 256 MB write between timed
+    # replays (timed with its own events and subtracted).
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn(torch.cuda.current_stream(dev).cuda_stream)
+        return g
+
+    def flush_needed():
+        return sum(h.numel() * h.element_size() for h in dw.hidden) < (256 << 20)
+
+    need_flush = flush_needed()
+    workload_cfg["l2"] = (
+        "a search's hidden states fit in L2: a 256 MB buffer is written before every timed "
+        "replay (its time subtracted)" if need_flush else
+        "inputs larger than L2 (hidden states >= 0.47 GB per level), no flush")
+    workload_cfg["timing"] = ("one search captured as a CUDA graph and replayed; per-level "
+                              "times from graphs of each launch")
+    if need_flush and flush is None:
+        flush = torch.empty((256 << 20,), dtype=torch.uint8, device=dev)
+    g_search = capture(lambda sp: one_search(sp=sp, gather=False))
+    g_step, g_merge = [], []
+    for level in range(w.levels):
+        cur_l = None if level == 0 else curs[level]
+        if w.sampling:
+            g_step.append(capture(lambda sp, l=level, c=cur_l: L.check(
+                lib.vtnk_fused_linear_constrained_node_transition_sampling_ix(
+                    lins[l], L.ptr(c), csr, dw.trie.layer_max_branches[l], w.seed,
+                    temp_t.data_ptr(), idxs[l], None, None, samp_out[l][0].data_ptr(),
+                    samp_out[l][1].data_ptr(), sp))))
+            g_merge.append(None)
+        else:
+            g_step.append(capture(lambda sp, l=level, c=cur_l: step_launch(l, c, sp)))
+            prev = (None, None) if level == 0 else (bufs[level - 1]["logp"], bufs[level - 1]["ids"])
+            g_merge.append(capture(lambda sp, l=level, pv=prev: merge_launch(l, pv[0], pv[1], sp)))
+    torch.cuda.synchronize(dev)
+
+    def replay_timed(g, n):
+        """Mean device ms of n replays of g (flushing L2 before each when needed)."""
+        evs = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(2)) for _ in range(n)]
+        for e0, e1 in evs:
+            if need_flush:
+                flush.fill_(1)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize(dev)
+        return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
         dist.barrier()
@@ -410,18 +463,25 @@ def main():
     fev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(2))
            for _ in range(args.steps)]
     t_start.record(stream)
-    for s in range(args.steps):
-        one_search(ev[s], fev[s] if w.sampling else None)
+    for s_ in range(args.steps):
+        if need_flush:
+            fev[s_][0].record(stream)
+            flush.fill_(1)
+            fev[s_][1].record(stream)
+        g_search.replay()
+        if world > 1 and not w.sampling:
+            gather_results(bufs[-1]["ids"], bufs[-1]["logp"], bufs[-1]["nxt"], out=gather_out)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     clk = clocks.stop()
     ms_total = t_start.elapsed_time(t_end)
-    if w.sampling:
+    if need_flush:
         ms_total -= sum(f[0].elapsed_time(f[1]) for f in fev)
-    step_ms = [[ev[s][l][0].elapsed_time(ev[s][l][1]) for l in range(w.levels)]
-               for s in range(args.steps)]
+    n_lvl = max(3, min(args.steps, 30))
+    lvl_ms = [replay_timed(g, n_lvl) for g in g_step]
+    merge_ms = [0.0 if g is None else replay_timed(g, n_lvl) for g in g_merge]
     t = torch.tensor([ms_total], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -431,7 +491,6 @@ def main():
 
     # roofline of the step kernel (all levels): algorithmic bytes / event time
     hbm_peak, tc_peak, peak_kind = _peaks()
-    lvl_ms = [statistics.mean(step_ms[s][l] for s in range(args.steps)) for l in range(w.levels)]
     tot_bytes = sum(c[0] for c in costs)
     tot_flops = sum(c[1] for c in costs)
     t_step = sum(lvl_ms) / 1e3
@@ -454,9 +513,7 @@ def main():
     roof["tensor_frac"] = (tot_flops / t_step / 1e12) / tc_peak
     roof["hbm_frac"] = (tot_bytes / t_step / 1e9) / hbm_peak
     roof["per_level_ms"] = [round(x, 4) for x in lvl_ms]
-    roof["merge_ms"] = [round(statistics.mean(ev[s][l][1].elapsed_time(ev[s][l][2])
-                                              for s in range(args.steps)), 4)
-                        for l in range(w.levels)]
+    roof["merge_ms"] = [round(x, 4) for x in merge_ms]
     roof["per_level_alg_bytes"] = [c[0] for c in costs]
     roof["per_level_alg_flops"] = [c[1] for c in costs]
     roof["roofline_ms"] = round(max(t_hbm, t_tc) * 1e3, 4)

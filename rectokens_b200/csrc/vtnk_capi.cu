@@ -3,6 +3,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <cstdlib>
+#include <mutex>
 
 #include "vtnk_common.cuh"
 #include "vtnk_internal.h"
@@ -24,6 +26,57 @@ int cuda_status(cudaError_t e, const char* what) {
   if (e == cudaSuccess) return VTNK_OK;
   set_error("%s: %s", what, cudaGetErrorString(e));
   return VTNK_ERR_CUDA;
+}
+
+SkWorkspace sk_workspace(cudaStream_t s) {
+  struct Entry {
+    int dev;
+    cudaStream_t stream;
+    SkWorkspace w;
+  };
+  constexpr int kMaxEntries = 16;  // streams with a workspace; others run whole tiles only
+  static std::mutex mu;
+  static Entry entries[kMaxEntries];
+  static int n_entries = 0;
+  // Opt-in (VTNK_STREAMK=1): on B200 the split-tile hand-over measured
+  // slower than whole-tile rounds for every configuration tried.
+  static const bool enabled = [] {
+    const char* e = getenv("VTNK_STREAMK");
+    return e && e[0] == '1';
+  }();
+  SkWorkspace none{};
+  int dev = 0;
+  if (!enabled || cudaGetDevice(&dev) != cudaSuccess) return none;
+  std::lock_guard<std::mutex> lock(mu);
+  Entry* e = nullptr;
+  for (int i = 0; i < n_entries; ++i)
+    if (entries[i].dev == dev && entries[i].stream == s) e = &entries[i];
+  if (!e) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (n_entries == kMaxEntries || cudaStreamIsCapturing(s, &cs) != cudaSuccess ||
+        cs != cudaStreamCaptureStatusNone)
+      return none;  // no allocation inside a graph capture
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    SkWorkspace w{};
+    w.cap_pairs = sms / 2;
+    w.count_cap = 4 * w.cap_pairs;  // fewer than 2 * pairs split tiles, 2 ranks each
+    const size_t part_bytes = static_cast<size_t>(w.cap_pairs) * 2 * 2 * 128 * 256 * 4;
+    if (cudaMalloc(&w.part, part_bytes) != cudaSuccess) {
+      cudaGetLastError();
+      return none;
+    }
+    if (cudaMalloc(&w.count, w.count_cap * sizeof(unsigned long long)) != cudaSuccess ||
+        cudaMemset(w.count, 0, w.count_cap * sizeof(unsigned long long)) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(w.part);
+      return none;
+    }
+    entries[n_entries] = Entry{dev, s, w};
+    e = &entries[n_entries++];
+  }
+  if (++e->w.epoch == 0) e->w.epoch = 1;
+  return e->w;
 }
 
 namespace {
@@ -116,7 +169,7 @@ SearchLayout search_layout(const vtnk_search_t* s) {
 int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr, int64_t mb,
             int64_t n_cand, const vtnk_child_index_t* index, int64_t* cand_tok,
             float* cand_logit, int64_t* cand_node, float* row_lse, int sample, uint64_t seed,
-            const float* temperature, float* sample_f, cudaStream_t s) {
+            const float* temperature, float* sample_f, bool stream_k, cudaStream_t s) {
   if (tc_enabled() && index && index->masks && lin->dtype == VTNK_BF16 && lin->b_stride_k == 1 &&
       lin->rows >= 128) {
     TcArgs t{};
@@ -145,6 +198,14 @@ int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t*
     t.seed = seed;
     t.temperature = temperature;
     t.sample_f = sample_f;
+    if (stream_k) {
+      const SkWorkspace w = sk_workspace(s);
+      t.sk_part = w.part;
+      t.sk_count = w.count;
+      t.sk_cap_pairs = w.cap_pairs;
+      t.sk_count_cap = w.count_cap;
+      t.sk_epoch = w.epoch;
+    }
     return launch_beam_step_tc(t, s);
   }
   return VTNK_ERR_UNSUPPORTED;
@@ -154,10 +215,10 @@ int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t*
 int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
                    int64_t mb, int64_t n_cand, const vtnk_child_index_t* index,
                    int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
-                   cudaStream_t s) {
+                   bool stream_k, cudaStream_t s) {
   if (lin->rows == 0) return VTNK_OK;
   const int rc = tc_step(lin, cur_node, csr, mb, n_cand, index, cand_tok, cand_logit, cand_node,
-                         row_lse, 0, 0, nullptr, nullptr, s);
+                         row_lse, 0, 0, nullptr, nullptr, stream_k, s);
   if (rc != VTNK_ERR_UNSUPPORTED) return rc;
   RowsArgs p = rows_from(lin, cur_node, csr, mb);
   p.k = static_cast<int>(n_cand);
@@ -265,7 +326,7 @@ int vtnk_fused_linear_constrained_node_transition_topk_ix(
   if (lin->rows == 0) return VTNK_OK;
   cudaStream_t s = as_stream(stream);
   rc = tc_step(lin, cur_node, csr, max_branches, k, index, topk_idxs, topk_logits, nullptr,
-               nullptr, 0, 0, nullptr, nullptr, s);
+               nullptr, 0, 0, nullptr, nullptr, true, s);
   if (rc == VTNK_ERR_UNSUPPORTED) {
     RowsArgs p = rows_from(lin, cur_node, csr, max_branches);
     p.k = static_cast<int>(k);
@@ -294,7 +355,7 @@ int vtnk_fused_linear_constrained_node_transition_sampling_ix(
   if (lin->rows == 0) return VTNK_OK;
   cudaStream_t s = as_stream(stream);
   rc = tc_step(lin, cur_node, csr, max_branches, 1, index, nullptr, nullptr, sample_node, nullptr,
-               1, seed, temperature, sample, s);
+               1, seed, temperature, sample, true, s);
   if (rc == VTNK_ERR_UNSUPPORTED) {
     RowsArgs p = rows_from(lin, cur_node, csr, max_branches);
     p.seed = seed;
@@ -344,7 +405,7 @@ int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk
   VTNK_REQUIRE(lin->rows == 0 || (cand_tok && cand_logit && cand_node && row_lse),
                "NULL pointer");
   return beam_step_impl(lin, cur_node, csr, max_branches, n_cand, index, cand_tok, cand_logit,
-                        cand_node, row_lse, as_stream(stream));
+                        cand_node, row_lse, true, as_stream(stream));
 }
 
 int vtnk_beam_merge(int64_t level, int64_t B, int64_t k, int64_t n_cand,
@@ -384,6 +445,15 @@ size_t vtnk_beam_search_workspace_bytes(const vtnk_search_t* s) {
 
 int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_bytes,
                      int64_t* out_ids, float* out_logp, int64_t* out_node, void* stream) {
+  return beam_search_run(s, workspace, workspace_bytes, out_ids, out_logp, out_node, stream, true);
+}
+
+}  // extern "C"
+
+namespace vtnk {
+int beam_search_run(const vtnk_search_t* s, void* workspace, size_t workspace_bytes,
+                    int64_t* out_ids, float* out_logp, int64_t* out_node, void* stream,
+                    bool stream_k) {
   VTNK_REQUIRE(s != nullptr, "search is NULL");
   VTNK_REQUIRE(s->levels >= 1 && s->batch >= 0 && s->beams >= 1 && s->n_cand >= 1,
                "bad search sizes");
@@ -424,7 +494,7 @@ int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_b
     if (rc) return rc;
     const vtnk_child_index_t* idx = s->index ? &s->index[level] : nullptr;
     rc = beam_step_impl(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand, idx,
-                        cand_tok, cand_logit, cand_node, lse, st);
+                        cand_tok, cand_logit, cand_node, lse, stream_k, st);
     if (rc) return rc;
     const bool last = level + 1 == s->levels;
     const int slot = static_cast<int>(level & 1);
@@ -440,6 +510,9 @@ int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_b
   }
   return VTNK_OK;
 }
+}  // namespace vtnk
+
+extern "C" {
 
 int vtnk_device_status(int reset) {
   const cudaError_t e = cudaDeviceSynchronize();

@@ -73,7 +73,28 @@ struct TcArgs {
   uint64_t seed;
   const float* temperature;  // device scalar or nullptr (1)
   float* sample_f;           // optional: sampled token id as float, -1 when none
+  // Stream-K workspace (all nullptr: whole tiles round-robin only).
+  float* sk_part;                // sk_cap_pairs * 512 KB
+  unsigned long long* sk_count;  // sk_count_cap words, zero before first use
+  int64_t sk_cap_pairs, sk_count_cap;
+  uint32_t sk_epoch;             // distinct per launch on this workspace, never 0
 };
+
+// Stream-K workspace of the library for (current device, stream): allocated
+// on first use and kept; nullptr members when it cannot be had.
+struct SkWorkspace {
+  float* part;
+  unsigned long long* count;
+  int64_t cap_pairs, count_cap;
+  uint32_t epoch;  // of this launch
+};
+SkWorkspace sk_workspace(cudaStream_t s);
+
+// vtnk_beam_search with stream-K scheduling optional (off: no library
+// workspace is allocated, for the allocation-free entry point).
+int beam_search_run(const vtnk_search_t* s, void* workspace, size_t workspace_bytes,
+                    int64_t* out_ids, float* out_logp, int64_t* out_node, void* stream,
+                    bool stream_k);
 
 int launch_rows(const RowsArgs& p, int mode, int dtype, cudaStream_t s);
 int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,

@@ -67,6 +67,8 @@ extern "C" int vtnk_beam_search_noalloc(const vtnk_search_t* s, int64_t* out_ids
   if (rc) return rc;
   // Every scratch byte the search reads is written earlier in the same call,
   // so nothing needs clearing between calls.
-  return vtnk_beam_search(s, scratch, VTNK_NOALLOC_SCRATCH_BYTES, out_ids, out_logp, out_node,
-                          stream);
+  // Whole-tile scheduling only: stream-K would allocate the library's
+  // workspace on first use.
+  return beam_search_run(s, scratch, VTNK_NOALLOC_SCRATCH_BYTES, out_ids, out_logp, out_node,
+                         stream, false);
 }

@@ -26,6 +26,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <climits>
 #include <cstdlib>
 #include <mutex>
@@ -58,9 +59,9 @@ constexpr int PAIR_M = 2 * BM;  // rows per CTA pair (one cta_group::2 MMA tile)
 #define VTNK_TC_STAGES 5
 #endif
 constexpr int STAGES = VTNK_TC_STAGES;
-// Column groups of the epilogue's lower bound (16 or 32; 32 whenever NC > 16).
+// Column groups of the epilogue's lower bound for NC up to this many (a power of two).
 #ifndef VTNK_TC_GROUPS
-#define VTNK_TC_GROUPS 32
+#define VTNK_TC_GROUPS 16
 #endif
 constexpr int A_BYTES = BM * BK * 2;        // this CTA's 128 rows
 constexpr int B_BYTES = (BN / 2) * BK * 2;  // this CTA's half of the 256 window rows
@@ -84,8 +85,10 @@ struct Shared {
   uint64_t merge_full[4];
   uint64_t merge_empty[4];
   uint64_t mma_done;
+  uint64_t epi_sync;  // the epilogue warps of this CTA (split-tile hand-over)
   uint32_t tmem_base;
   int abort;
+  int sk_last;  // epilogue: this CTA finishes the current split tile
 };
 constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
 
@@ -112,6 +115,16 @@ struct Params {
   uint64_t seed;             // sampling: Philox key
   const float* temperature;  // sampling: device scalar (nullptr: 1)
   float* sample_f;           // sampling: token id as float, -1 when none (optional)
+  // Schedule: tiles [0, dp_tiles) go to pairs round-robin (whole tiles); the
+  // k-block iterations of tiles [dp_tiles, n_tiles) are split evenly over the
+  // first sk_pairs pairs (stream-K).  A tile split between pairs is summed
+  // from fp32 partials by its last contributor.
+  int64_t dp_tiles;
+  int64_t sk_iters;                  // (n_tiles - dp_tiles) * k-blocks
+  int sk_pairs;                      // 0: no stream-K part
+  float* sk_part;                    // [sk_pairs][2 slots][2 ranks][BM][BN] fp32
+  unsigned long long* sk_count;      // [stream-K tiles][2 ranks]: epoch << 32 | k-blocks done
+  uint32_t sk_epoch;                 // distinct per launch on the same workspace
 };
 
 // ------------------------------------------------------------------ PTX wrappers
@@ -351,6 +364,87 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// ------------------------------------------------------------------ schedule
+// One unit of a pair's work: k-blocks [kb0, kb1) of a 256-row tile.
+struct Seg {
+  int64_t tile;
+  int kb0, kb1;
+  int64_t sk_tile;  // index among the stream-K tiles, -1 for a round-robin tile
+  int slot;         // 0: the pair's first stream-K segment, 1: a later one
+};
+
+__device__ __forceinline__ int64_t sk_begin(const Params& p, int64_t q) {
+  return (q * p.sk_iters) / p.sk_pairs;
+}
+// The pair whose stream-K range holds iteration g.
+__device__ __forceinline__ int64_t sk_owner(const Params& p, int64_t g) {
+  return ((g + 1) * p.sk_pairs + p.sk_iters - 1) / p.sk_iters - 1;
+}
+
+// Enumerates a pair's segments in order; producer, MMA issuer and epilogue
+// walk the same sequence.  Small state: it lives through the whole kernel.
+struct SegIter {
+  int64_t g, gend;  // stream-K iteration cursor and end
+  int i;            // round-robin tiles taken
+  int pair;
+  bool first;       // the next stream-K segment is the pair's first
+  __device__ __forceinline__ void init(const Params& p, int pr) {
+    i = 0;
+    pair = pr;
+    first = true;
+    g = gend = 0;
+    if (pr < p.sk_pairs) {
+      g = sk_begin(p, pr);
+      gend = sk_begin(p, pr + 1);
+    }
+  }
+  __device__ __forceinline__ bool next(const Params& p, int kblocks, int64_t n_pairs, Seg& s) {
+    const int64_t t = pair + static_cast<int64_t>(i) * n_pairs;
+    if (t < p.dp_tiles) {
+      ++i;
+      s.tile = t;
+      s.kb0 = 0;
+      s.kb1 = kblocks;
+      s.sk_tile = -1;
+      s.slot = 0;
+      return true;
+    }
+    if (g < gend) {
+      s.sk_tile = g / kblocks;
+      s.tile = p.dp_tiles + s.sk_tile;
+      s.kb0 = static_cast<int>(g - s.sk_tile * kblocks);
+      const int64_t left = gend - g;
+      s.kb1 = left < kblocks - s.kb0 ? s.kb0 + static_cast<int>(left) : kblocks;
+      s.slot = first ? 0 : 1;
+      first = false;
+      g += s.kb1 - s.kb0;
+      return true;
+    }
+    return false;
+  }
+};
+
+// Adds `add` k-blocks to a split tile's counter; true for the contributor
+// that completes the tile (which then resets the counter).  Values tagged
+// with another launch's epoch count as zero.
+__device__ __forceinline__ bool sk_arrive(unsigned long long* w, uint32_t epoch, int add,
+                                          int kblocks) {
+  unsigned long long old = atomicAdd(w, 0ull), seen;
+  uint32_t done = 0;
+  for (int tries = 0; tries < (1 << 20); ++tries) {
+    const uint32_t have = (static_cast<uint32_t>(old >> 32) == epoch) ? static_cast<uint32_t>(old)
+                                                                       : 0u;
+    done = have + static_cast<uint32_t>(add);
+    const unsigned long long nv = (static_cast<unsigned long long>(epoch) << 32) | done;
+    seen = atomicCAS(w, old, nv);
+    if (seen == old) break;
+    old = seen;
+  }
+  if (done != static_cast<uint32_t>(kblocks)) return false;
+  atomicExch(w, 0ull);
+  return true;
+}
+
 // ------------------------------------------------------------------ per-row selection
 template <int NC>
 struct TopN {
@@ -453,6 +547,65 @@ __device__ __forceinline__ void load_chunk(uint32_t taddr, int chunk, const uint
   }
 }
 
+// Partial accumulators of split tiles: per (pair, slot, rank) a [BM, BN]
+// fp32 block stored as [chunk][vec][row][4] so that a warp's 16-byte
+// accesses to one (chunk, vec) are 512 contiguous bytes.
+__device__ __forceinline__ float4* part_at(const Params& p, int64_t q, int slot, uint32_t rank,
+                                           int chunk, int vec, int r_local) {
+  return reinterpret_cast<float4*>(p.sk_part) +
+         ((q * 2 + slot) * 2 + rank) * (BM * BN / 4) + (chunk * 8 + vec) * BM + r_local;
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+      "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]),
+      "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]),
+      "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]),
+      "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// The finisher of a split tile: the sum of every contributor's partial
+// (contributors in pair order, so the result does not depend on which pair
+// finishes) replaces this warp's 32 rows x 128 columns of the TMEM buffer.
+__device__ __forceinline__ void sum_partials_to_tmem(const Params& p, int64_t sk_tile, int kblocks,
+                                                  uint32_t rank, int r_local, int c0,
+                                                  uint32_t taddr) {
+  const int64_t q0 = sk_owner(p, sk_tile * kblocks);
+  const int64_t q1 = sk_owner(p, (sk_tile + 1) * kblocks - 1);
+#pragma unroll 1
+  for (int ci = 0; ci < BN / 64; ++ci) {
+    const int chunk = c0 + ci;
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+#pragma unroll 1
+    for (int64_t q = q0; q <= q1; ++q) {
+      const int slot = (sk_begin(p, q) / kblocks == sk_tile) ? 0 : 1;
+      float4 f[8];
+#pragma unroll
+      for (int v = 0; v < 8; ++v) f[v] = __ldcg(part_at(p, q, slot, rank, chunk, v, r_local));
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        acc[4 * v] += f[v].x;
+        acc[4 * v + 1] += f[v].y;
+        acc[4 * v + 2] += f[v].z;
+        acc[4 * v + 3] += f[v].w;
+      }
+    }
+    uint32_t u[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(acc[i]);
+    __syncwarp();
+    tmem_st32(taddr + chunk * 32, u);
+  }
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
 // Exact per-row path for a row whose node is outside the index or whose
 // children are not a clean sorted in-window set (slow, never taken for a
 // sorted catalog trie queried at the right depth).
@@ -498,7 +651,6 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const uint32_t rank = cluster_rank();            // 0 = pair leader (issues the MMAs)
   const int64_t pair = blockIdx.x >> 1;
   const int64_t n_pairs = gridDim.x >> 1;
-  const int64_t n_tiles = (p.rows + PAIR_M - 1) / PAIR_M;  // 256-row tiles, one per pair step
   const int kblocks = static_cast<int>((p.H + BK - 1) / BK);
   volatile int* abort = &S.abort;
 
@@ -516,6 +668,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       mbar_init(&S.merge_empty[g], 32);
     }
     mbar_init(&S.mma_done, 1);
+    mbar_init(&S.epi_sync, EPI_WARPS);
     S.abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -552,9 +705,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       uint32_t phase = 0;
       bool ok = true;
       const int wrow = static_cast<int>(p.window_lo) + static_cast<int>(rank) * (BN / 2);
-      for (int64_t tile = pair; ok && tile < n_tiles; tile += n_pairs) {
-        const int arow = static_cast<int>(tile * PAIR_M) + static_cast<int>(rank) * BM;
-        for (int kb = 0; kb < kblocks; ++kb) {
+      SegIter seg;
+      seg.init(p, static_cast<int>(pair));
+      Seg sg;
+      while (ok && seg.next(p, kblocks, n_pairs, sg)) {
+        const int arow = static_cast<int>(sg.tile * PAIR_M) + static_cast<int>(rank) * BM;
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           PROF_T0(t_w);
           if (!wait_phase(&S.empty[stage], phase ^ 1, abort, 1)) {
             ok = false;
@@ -603,14 +759,17 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       uint32_t it = 0;
       bool ok = true;
       long long prof_full = 0, prof_tempty = 0;
-      for (int64_t tile = pair; ok && tile < n_tiles; tile += n_pairs, ++it) {
+      SegIter seg;
+      seg.init(p, static_cast<int>(pair));
+      Seg sg;
+      for (; ok && seg.next(p, kblocks, n_pairs, sg); ++it) {
         const uint32_t buf = it & 1;
         PROF_T0(t_e);
         if (!wait_phase_cluster(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)) break;
         PROF_ACC(prof_tempty, t_e);
         tc_fence_after();
         const uint32_t d = tmem + buf * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           PROF_T0(t_f);
           if (!wait_phase(&S.full[stage], phase, abort, 3)) {
             ok = false;
@@ -622,7 +781,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const uint64_t db = umma_desc_sw128(S.ring[stage] + A_BYTES);
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)  // +32 B per K=16 step inside the swizzle atom
-            umma_bf16(d, da + 2 * k, db + 2 * k, (kb | k) != 0);
+            umma_bf16(d, da + 2 * k, db + 2 * k, (kb != sg.kb0 || k != 0) ? 1u : 0u);
           umma_commit_pair(&S.empty[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -644,7 +803,22 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     uint32_t it = 0;
     long long pe_pro = 0, pe_wait = 0, pe_tmem = 0, pe_out = 0, pe_ld = 0;
     const uint32_t tempty_leader[2] = {map_to_rank(&S.tempty[0], 0), map_to_rank(&S.tempty[1], 0)};
-    for (int64_t tile = pair; tile < n_tiles; tile += n_pairs, ++it) {
+    uint32_t mit = 0;  // hand-offs between the two column halves so far
+    uint32_t eb = 0;   // epi_sync phases so far
+    // All epilogue warps of the CTA meet (bounded wait; false on abort).
+    auto epi_sync = [&]() {
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.epi_sync);
+      const bool ok = warp_wait_phase(&S.epi_sync, eb & 1, abort, 7);
+      if (ok) mbar_try_wait(&S.epi_sync, eb & 1);  // every lane acquires
+      ++eb;
+      return ok;
+    };
+    SegIter seg;
+    seg.init(p, static_cast<int>(pair));
+    Seg sg;
+    for (; seg.next(p, kblocks, n_pairs, sg); ++it) {
+      const int64_t tile = sg.tile;
       PROF_T0(t_pro);
       const int64_t row = tile * PAIR_M + static_cast<int64_t>(rank) * BM + r_local;
       const bool live = row < p.rows;
@@ -692,12 +866,47 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       continue;
 #endif
 
-      TopN<NC> top;
-      top.init();
-      float mx = -INFINITY, sum = 0.f;
       const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BN;
       const bool has_bias = p.bias != nullptr;
       const int c0 = half * (BN / 64);  // this warp's first 32-column chunk
+      // A segment that covers part of a tile stores its raw accumulator
+      // (this warp's 32 rows x 128 columns) as an fp32 partial and counts
+      // its k-blocks.  The contributor that completes the tile replaces its
+      // TMEM buffer by the sum of all partials and runs the epilogue; the
+      // others free the buffer.
+      if (sg.kb0 != 0 || sg.kb1 != kblocks) {
+        // This CTA's raw accumulator of the segment (coalesced fp32 partial).
+#pragma unroll 1
+        for (int ci = 0; ci < BN / 64; ++ci) {
+          uint32_t v[32];
+          __syncwarp();
+          tmem_ld32(taddr + (c0 + ci) * 32, v);
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(part_at(p, pair, sg.slot, rank, c0 + ci, q, r_local),
+                   make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                               __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])));
+        }
+        __threadfence();
+        if (!epi_sync()) break;
+        if (warp == 2 && lane == 0)
+          S.sk_last = sk_arrive(p.sk_count + sg.sk_tile * 2 + rank, p.sk_epoch,
+                                sg.kb1 - sg.kb0, kblocks) ? 1 : 0;
+        if (!epi_sync()) break;
+        const int finisher = *reinterpret_cast<volatile int*>(&S.sk_last);
+        if (!finisher) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);
+          continue;
+        }
+        __threadfence();
+        sum_partials_to_tmem(p, sg.sk_tile, kblocks, rank, r_local, c0, taddr);
+      }
+
+      TopN<NC> top;
+      top.init();
+      float mx = -INFINITY, sum = 0.f;
       const float temp = (SAMPLE && p.temperature) ? __ldg(p.temperature) : 1.f;
       if constexpr (SAMPLE) {
         // Gumbel-max over this half's children: score = logit / T + g, with
@@ -742,7 +951,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // group maximum is a lower bound of the NC-th largest value (the NC
         // largest group maxima are NC distinct entries), so pass 2 only inserts
         // values at or above it.
-        constexpr int G = NC <= VTNK_TC_GROUPS ? VTNK_TC_GROUPS : 32;
+        // G >= NC groups: 16 (the NC-th largest maximum by a sorting network)
+        // up to NC = 16, else NC groups (their smallest maximum).
+        constexpr int G = NC <= VTNK_TC_GROUPS ? VTNK_TC_GROUPS : NC;
         float gm[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) gm[g] = -INFINITY;
@@ -816,8 +1027,8 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // the same rows through shared memory; bounded waits on both sides.
       float (*mg)[32] = S.merge[lg];
       if (half == 1) {
-        if (!warp_wait_phase(&S.merge_empty[lg], (it & 1) ^ 1, abort, 5)) break;
-        mbar_try_wait(&S.merge_empty[lg], (it & 1) ^ 1);
+        if (!warp_wait_phase(&S.merge_empty[lg], (mit & 1) ^ 1, abort, 5)) break;
+        mbar_try_wait(&S.merge_empty[lg], (mit & 1) ^ 1);
 #pragma unroll
         for (int j = 0; j < NC; ++j) mg[j][lane] = top.v[j];
 #pragma unroll
@@ -832,11 +1043,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         mg[MAX_NC + MAX_NC / 4][lane] = mx;
         mg[MAX_NC + MAX_NC / 4 + 1][lane] = sum;
         mbar_arrive(&S.merge_full[lg]);
+        ++mit;
         PROF_ACC(pe_tmem, t_tm);
         continue;
       }
-      if (!warp_wait_phase(&S.merge_full[lg], it & 1, abort, 6)) break;
-      mbar_try_wait(&S.merge_full[lg], it & 1);
+      if (!warp_wait_phase(&S.merge_full[lg], mit & 1, abort, 6)) break;
+      mbar_try_wait(&S.merge_full[lg], mit & 1);
       {
         const float omx = mg[MAX_NC + MAX_NC / 4][lane];
         const float osum = mg[MAX_NC + MAX_NC / 4 + 1][lane];
@@ -855,6 +1067,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
       }
       mbar_arrive(&S.merge_empty[lg]);
+      ++mit;
 
       PROF_ACC(pe_tmem, t_tm);
       PROF_T0(t_out);
@@ -1001,21 +1214,32 @@ bool make_map(CUtensorMap* m, const void* base, uint64_t inner, uint64_t outer,
 }
 
 int sm_count() {
-  int dev = 0, n = 148;
+  constexpr int kMaxDev = 64;
+  static std::atomic<int> cached[kMaxDev] = {};
+  int dev = 0;
   cudaGetDevice(&dev);
+  if (dev >= 0 && dev < kMaxDev && cached[dev] > 0) return cached[dev];
+  int n = 148;
   cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  if (dev >= 0 && dev < kMaxDev) cached[dev] = n;
   return n;
 }
 
 template <int NC, bool SAMPLE = false>
-int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, cudaStream_t s) {
+int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, int pairs,
+              cudaStream_t s) {
   auto k = beam_step_kernel<NC, SAMPLE>;
-  cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                       static_cast<int>(SMEM_BYTES));
-  const int64_t pairs = (p.rows + PAIR_M - 1) / PAIR_M;  // one 256-row tile per pair step
-  const int max_pairs = sm_count() / 2;
-  const int grid = 2 * static_cast<int>(pairs < max_pairs ? pairs : max_pairs);
-  k<<<grid, THREADS, SMEM_BYTES, s>>>(a, w, p);
+  // The shared-memory opt-in is per kernel and device; set it once each.
+  static std::atomic<uint64_t> set_on{0};  // bit d: done on device d
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !((set_on.load(std::memory_order_relaxed) >> dev) & 1)) {
+    const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               static_cast<int>(SMEM_BYTES));
+    if (e != cudaSuccess) return cuda_status(e, "beam_step_tc smem attribute");
+    if (dev < 64) set_on.fetch_or(1ull << dev, std::memory_order_relaxed);
+  }
+  k<<<2 * pairs, THREADS, SMEM_BYTES, s>>>(a, w, p);
   return cuda_status(cudaGetLastError(), "beam_step_tc launch");
 }
 
@@ -1064,24 +1288,53 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.seed = t.seed;
   p.temperature = t.temperature;
   p.sample_f = t.sample_f;
+  // Schedule.  Whole tiles round-robin over the pairs; when the last round
+  // would leave pairs idle, the last two rounds' tiles are split into equal
+  // k-block ranges instead (at least MIN_SEG k-blocks per pair).
+  constexpr int64_t MIN_SEG = 4;
+  const int64_t n_tiles = (t.rows + PAIR_M - 1) / PAIR_M;
+  const int64_t kblocks = (t.H + BK - 1) / BK;
+  const int64_t max_pairs = sm_count() / 2;
+  int64_t pairs = n_tiles < max_pairs ? n_tiles : max_pairs;
+  p.dp_tiles = n_tiles;
+  p.sk_iters = 0;
+  p.sk_pairs = 0;
+  if (t.sk_part && t.sk_count && n_tiles % max_pairs != 0) {
+    const int64_t rounds = n_tiles / max_pairs;
+    const int64_t dp = rounds > 0 ? (rounds - 1) * max_pairs : 0;
+    const int64_t iters = (n_tiles - dp) * kblocks;
+    int64_t skp = iters / MIN_SEG;
+    if (skp > max_pairs) skp = max_pairs;
+    if (skp > t.sk_cap_pairs) skp = t.sk_cap_pairs;
+    if (skp >= 2 && 2 * (n_tiles - dp) <= t.sk_count_cap) {
+      p.dp_tiles = dp;
+      p.sk_iters = iters;
+      p.sk_pairs = static_cast<int>(skp);
+      p.sk_part = t.sk_part;
+      p.sk_count = t.sk_count;
+      p.sk_epoch = t.sk_epoch;
+      pairs = dp > 0 ? max_pairs : skp;
+    }
+  }
+  const int np = static_cast<int>(pairs);
   CUtensorMap ma, mw;
   if (!make_map(&ma, t.a, t.H, t.rows, t.a_stride * 2, BK, BM) ||
       !make_map(&mw, t.w, t.H, t.n_vocab, t.w_stride * 2, BK, BN / 2)) {
     set_error("cuTensorMapEncodeTiled failed");
     return VTNK_ERR_CUDA;
   }
-  if (t.sample) return t.n_cand == 1 ? launch_nc<1, true>(ma, mw, p, s) : VTNK_ERR_UNSUPPORTED;
+  if (t.sample) return t.n_cand == 1 ? launch_nc<1, true>(ma, mw, p, np, s) : VTNK_ERR_UNSUPPORTED;
   switch (t.n_cand) {  // exact widths for the common beam sizes
-    case 1: return launch_nc<1>(ma, mw, p, s);
-    case 5: return launch_nc<5>(ma, mw, p, s);
-    case 10: return launch_nc<10>(ma, mw, p, s);
-    case 20: return launch_nc<20>(ma, mw, p, s);
+    case 1: return launch_nc<1>(ma, mw, p, np, s);
+    case 5: return launch_nc<5>(ma, mw, p, np, s);
+    case 10: return launch_nc<10>(ma, mw, p, np, s);
+    case 20: return launch_nc<20>(ma, mw, p, np, s);
     default: break;
   }
-  if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, s);
-  if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, s);
-  if (t.n_cand <= 16) return launch_nc<16>(ma, mw, p, s);
-  return launch_nc<32>(ma, mw, p, s);
+  if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, np, s);
+  if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, np, s);
+  if (t.n_cand <= 16) return launch_nc<16>(ma, mw, p, np, s);
+  return launch_nc<32>(ma, mw, p, np, s);
 }
 
 int launch_build_child_index(const Csr& csr, uint32_t* masks, int64_t node_lo, int64_t node_hi,

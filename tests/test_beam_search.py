@@ -309,3 +309,45 @@ def test_sampling_search_cfg4_against_oracle(cuda_ok):
         cur = nxt
     np.testing.assert_array_equal(nd, cur)
     _device_status_ok()
+
+
+_SPLIT_CHECK = r"""
+import sys, torch
+sys.path.insert(0, "tests")
+from test_beam_search import _compare_steps, _device_status_ok
+from rectokens_b200 import synthetic as S, workload as WL
+from rectokens_b200.decoding.beam_search import beam_step
+w = S.WORKLOADS["cfg3"]
+dw = WL.make_device_workload(w, "cuda")
+cur = None
+for level, R in ((0, 700), (1, 3000)):
+    h = dw.hidden[level][:R]
+    a = beam_step(h, dw.weight, dw.trie, level, cur, 20)
+    for _ in range(3):
+        b = beam_step(h, dw.weight, dw.trie, level, cur, 20)
+        assert all(torch.equal(x, y) for x, y in zip(a, b)), "not deterministic"
+    ref = beam_step(h, dw.weight, dw.trie, level, cur, 20, index=None)
+    assert _compare_steps(a, ref) > 0.99
+    cur = ref[2][:, 0].repeat(5)[:3000]
+_device_status_ok()
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("stream_k", ["0", "1"])
+def test_tile_kernel_deterministic_and_split_tiles(stream_k, cuda_ok):
+    """Repeated launches give bit-identical results, with whole-tile rounds
+    and with the opt-in stream-K schedule (VTNK_STREAMK=1: tiles split
+    across SM pairs, fp32 partials summed by the last contributor in pair
+    order), and both match the row kernel.  Runs in a child process because
+    the schedule is chosen when the library loads."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, VTNK_STREAMK=stream_k, PYTHONPATH=str(root))
+    r = subprocess.run([sys.executable, "-c", _SPLIT_CHECK], cwd=root, env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
