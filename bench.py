@@ -287,7 +287,7 @@ def main():
     torch.cuda.set_device(dev)
 
     from rectokens_b200 import workload as WL
-    from rectokens_b200.distributed import gather_results
+    from rectokens_b200.distributed import ResultRecord
     from rectokens_b200.decoding.beam_search import (
         beam_merge,
         beam_step,
@@ -323,11 +323,12 @@ def main():
     lins = [L.linear_struct(dw.hidden[l], dw.weight.T, None) for l in range(w.levels)]
     stream = torch.cuda.current_stream(dev)
     sptr = stream.cuda_stream
-    gather_out = None
-    if world > 1:
-        gather_out = (torch.empty((w.batch * k, w.levels), dtype=torch.int64, device=dev),
-                      torch.empty((w.batch * k,), dtype=torch.float32, device=dev),
-                      torch.empty((w.batch * k,), dtype=torch.int64, device=dev))
+    # the last level writes its results straight into this rank's packed
+    # record, which one all-gather concatenates across ranks
+    rec = ResultRecord(Bq * k, w.levels, dev)
+    bufs[-1]["ids"], bufs[-1]["logp"], bufs[-1]["nxt"] = rec.ids, rec.logp, rec.node
+    gather_buf = (torch.empty((world * rec.nbytes,), dtype=torch.uint8, device=dev)
+                  if world > 1 else None)
 
     temp_t = torch.tensor([w.temperature], dtype=torch.float32, device=dev)
     samp_out = [(torch.empty((R,), dtype=torch.float32, device=dev),
@@ -383,7 +384,7 @@ def main():
                 events[level][2].record(stream)
             cur, prev_logp, prev_ids = b["nxt"], b["logp"], b["ids"]
         if world > 1 and gather:
-            gather_results(prev_ids, prev_logp, cur, out=gather_out)
+            rec.gather(out=gather_buf)
         return cur
 
     # warm-up (also records the per-level node arrays for the cost model); the
@@ -470,7 +471,7 @@ def main():
             fev[s_][1].record(stream)
         g_search.replay()
         if world > 1 and not w.sampling:
-            gather_results(bufs[-1]["ids"], bufs[-1]["logp"], bufs[-1]["nxt"], out=gather_out)
+            rec.gather(out=gather_buf)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:

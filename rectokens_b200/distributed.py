@@ -4,8 +4,14 @@ Queries are independent, so the batch shards into contiguous query ranges:
 every rank holds the full trie and head rows, generates (or receives) the
 hidden states of its own queries -- global row ``q`` at level 0 and rows
 ``q*k .. q*k+k-1`` after -- runs the search locally, and the per-rank results
-are concatenated with one all-gather per result tensor (NCCL over NVLink on
-GPUs; gloo works the same way on CPU tensors).  There is no other exchange.
+are concatenated with one all-gather (NCCL over NVLink on GPUs; gloo works
+the same way on CPU tensors).  There is no other exchange.
+
+The three result tensors of a rank travel as one packed record
+``[ids int64 (b*k*L) | node int64 (b*k) | logp fp32 (b*k), padded to 16 B]``
+so that the gather is a single collective: ``ResultRecord`` allocates a
+rank's tensors as views of its record (the search writes them in place, no
+packing copy) and the gathered buffer is read through rank-strided views.
 """
 
 from __future__ import annotations
@@ -30,15 +36,67 @@ def level_rows(first_query: int, n_queries: int, level: int, beams: int) -> tupl
     return first_query * per_q, n_queries * per_q
 
 
+class ResultRecord:
+    """One rank's search results ``(ids (n, L) int64, logp (n,) fp32, node (n,)
+    int64)`` as views of a single byte buffer, ``n = b*k`` rows."""
+
+    def __init__(self, n: int, levels: int, device):
+        self.n, self.levels = n, levels
+        self.ids_bytes = n * levels * 8
+        self.node_bytes = n * 8
+        self.logp_bytes = n * 4
+        used = self.ids_bytes + self.node_bytes + self.logp_bytes
+        self.nbytes = (used + 15) // 16 * 16
+        self.buf = torch.zeros((self.nbytes,), dtype=torch.uint8, device=device)
+        self.ids, self.node, self.logp = self.views(self.buf.view(1, -1))
+        self.ids, self.node, self.logp = self.ids[0], self.node[0], self.logp[0]
+
+    def views(self, rec: torch.Tensor):
+        """``(ids (R, n, L), node (R, n), logp (R, n))`` views of ``R`` records
+        laid out back to back (``rec``: ``(R, nbytes)`` uint8)."""
+        a, b = self.ids_bytes, self.ids_bytes + self.node_bytes
+        ids = rec[:, :a].view(torch.int64).view(rec.shape[0], self.n, self.levels)
+        node = rec[:, a:b].view(torch.int64)
+        logp = rec[:, b:b + self.logp_bytes].view(torch.float32)
+        return ids, node, logp
+
+    def gather(self, group=None, out: torch.Tensor | None = None):
+        """All-gather the records of every rank (one collective).  Returns
+        ``(ids (world, n, L), logp (world, n), node (world, n))`` views of the
+        gathered buffer; rank r's rows are queries of shard r, in order."""
+        world = dist.get_world_size(group)
+        if out is None:
+            out = self.buf.new_empty((world * self.nbytes,))
+        dist.all_gather_into_tensor(out, self.buf, group=group)
+        ids, node, logp = self.views(out.view(world, self.nbytes))
+        return ids, logp, node
+
+
 def gather_results(ids: torch.Tensor, logp: torch.Tensor, node: torch.Tensor, group=None,
                    out=None):
     """All-gather each rank's ``(ids (b*k, L), logp (b*k,), node (b*k,))`` into the
-    full-batch tensors in rank order (pre-allocated ``out`` may be passed)."""
+    full-batch tensors in rank order (pre-allocated ``out`` may be passed).
+    The three tensors are packed into one record and gathered with a single
+    collective."""
     world = dist.get_world_size(group)
+    if (ids.dtype, logp.dtype, node.dtype) != (torch.int64, torch.float32, torch.int64):
+        if out is None:  # other dtypes: one collective per tensor
+            out = (ids.new_empty((ids.shape[0] * world,) + tuple(ids.shape[1:])),
+                   logp.new_empty((logp.shape[0] * world,)),
+                   node.new_empty((node.shape[0] * world,)))
+        for dst, src in zip(out, (ids, logp, node)):
+            dist.all_gather_into_tensor(dst, src.contiguous(), group=group)
+        return out
+    rec = ResultRecord(ids.shape[0], ids.shape[1], ids.device)
+    rec.ids.copy_(ids)
+    rec.logp.copy_(logp)
+    rec.node.copy_(node)
+    g_ids, g_logp, g_node = rec.gather(group)
     if out is None:
         out = (ids.new_empty((ids.shape[0] * world,) + tuple(ids.shape[1:])),
                logp.new_empty((logp.shape[0] * world,)),
                node.new_empty((node.shape[0] * world,)))
-    for dst, src in zip(out, (ids, logp, node)):
-        dist.all_gather_into_tensor(dst, src.contiguous(), group=group)
+    out[0].view(world, ids.shape[0], -1).copy_(g_ids)
+    out[1].view(world, -1).copy_(g_logp)
+    out[2].view(world, -1).copy_(g_node)
     return out

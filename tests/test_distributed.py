@@ -49,6 +49,20 @@ def _worker(rank, world, port, q):
         ids, logp, node = O.beam_search(_inputs(w, q0, nq), W, rp, cv, lmb, nq, w.beams, w.topk)
         out = D.gather_results(torch.from_numpy(ids.reshape(nq * w.beams, -1)),
                                torch.from_numpy(logp), torch.from_numpy(node))
+        # the packed single-collective path (fp32 log-probs)
+        lp32 = torch.from_numpy(logp).float()
+        out32 = D.gather_results(torch.from_numpy(ids.reshape(nq * w.beams, -1)), lp32,
+                                 torch.from_numpy(node))
+        rec = D.ResultRecord(nq * w.beams, w.levels, "cpu")
+        rec.ids.copy_(torch.from_numpy(ids.reshape(nq * w.beams, -1)))
+        rec.logp.copy_(lp32)
+        rec.node.copy_(torch.from_numpy(node))
+        r_ids, r_logp, r_node = rec.gather()
+        assert torch.equal(r_ids.reshape(-1, w.levels), out32[0])
+        assert torch.equal(r_logp.reshape(-1), out32[1])
+        assert torch.equal(r_node.reshape(-1), out32[2])
+        assert torch.equal(out32[0], out[0]) and torch.equal(out32[2], out[2])
+        assert torch.equal(out32[1], out[1].float())
         if rank == 0:
             full = O.beam_search(_inputs(w, 0, w.batch), W, rp, cv, lmb, w.batch, w.beams, w.topk)
             q.put((out[0].numpy(), out[1].numpy(), out[2].numpy(),
