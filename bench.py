@@ -4,11 +4,15 @@
 
 A step = one full L-level constrained beam search over this rank's shard of
 the workload (config 5 by default: 16M-item catalog, H=3584, bf16, batch
-65,536 x 10 beams, top-k 10), plus -- for N > 1 -- the NCCL all-gather of every
-rank's results.  Inputs (trie, head rows, per-level hidden states) are resident
-in HBM before timing; the hidden states (10 GB at N=1) exceed the 126 MB L2, so
-no flush is needed between steps.  value = (sum over levels of rows) * N /
-(max over ranks of the device time per step).
+65,536 x 10 beams, top-k 10; `--workload cfg4` is the Gumbel-max sampled
+search), plus -- for N > 1 -- the NCCL all-gather of every rank's results.
+Inputs (trie, head rows, per-level hidden states) are resident in HBM before
+timing.  One search is captured as a CUDA graph and replayed K times after W
+warm-ups, timed with CUDA events on the launching stream.  At config 5 the
+hidden states (10 GB at N=1) exceed the 126 MB L2; smaller workloads get a
+256 MB write before every timed replay (timed separately and subtracted).
+value = (sum over levels of rows) * N / (max over ranks of the device time
+per step).
 
 `e2e` runs the same search through the public API with the hidden states in
 pinned host memory, host->device copies (overlapped with compute) and the
@@ -335,19 +339,13 @@ def main():
                  torch.empty((R,), dtype=torch.int64, device=dev)) for R in rows_l]
     flush = None
 
-    def one_sampled(events=None, sp=None):
-        sp = sptr if sp is None else sp
+    def one_sampled(sp):
         cur = None
         for level in range(w.levels):
             smp, nd = samp_out[level]
-            if events is not None:
-                events[level][0].record(stream)
             L.check(lib.vtnk_fused_linear_constrained_node_transition_sampling_ix(
                 lins[level], L.ptr(cur), csr, dw.trie.layer_max_branches[level], w.seed,
                 temp_t.data_ptr(), idxs[level], None, None, smp.data_ptr(), nd.data_ptr(), sp))
-            if events is not None:
-                events[level][1].record(stream)
-                events[level][2].record(stream)
             cur = nd
         return cur
 
@@ -367,21 +365,15 @@ def main():
                                     b["ids"].data_ptr(), b["logp"].data_ptr(),
                                     b["nxt"].data_ptr(), b["parent"].data_ptr(), sp))
 
-    def one_search(events=None, sp=None, gather=True):
+    def one_search(sp=None, gather=True):
         sp = sptr if sp is None else sp
         if w.sampling:
-            return one_sampled(events, sp)
+            return one_sampled(sp)
         cur = prev_logp = prev_ids = None
         for level in range(w.levels):
             b = bufs[level]
-            if events is not None:
-                events[level][0].record(stream)
             step_launch(level, cur, sp)
-            if events is not None:
-                events[level][1].record(stream)
             merge_launch(level, prev_logp, prev_ids, sp)
-            if events is not None:
-                events[level][2].record(stream)
             cur, prev_logp, prev_ids = b["nxt"], b["logp"], b["ids"]
         if world > 1 and gather:
             rec.gather(out=gather_buf)

@@ -165,9 +165,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatil
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
   for (uint32_t i = 1;; ++i) {
-#ifndef VTNK_TC_NOSLEEP
     if (ns) __nanosleep(ns);  // back off so a waiting role does not steal issue slots
-#endif
     if (mbar_try_wait(b, parity)) return true;
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
@@ -218,9 +216,7 @@ __device__ __forceinline__ bool wait_phase_cluster(uint64_t* b, uint32_t parity,
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
   for (uint32_t i = 1;; ++i) {
-#ifndef VTNK_TC_NOSLEEP
     if (ns) __nanosleep(ns);
-#endif
     if (mbar_try_wait_cluster(b, parity)) return true;
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
@@ -243,27 +239,6 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
       "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y)
       : "memory");
 }
-// Same, with an L2 eviction-priority policy (createpolicy).
-__device__ __forceinline__ void tma_load_2d_pair_hint(void* dst, const CUtensorMap* map,
-                                                      uint32_t leader_bar, int x, int y,
-                                                      uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(su32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_bar), "r"(x), "r"(y), "l"(policy)
-      : "memory");
-}
-__device__ __forceinline__ uint64_t policy_evict_first() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-__device__ __forceinline__ uint64_t policy_evict_last() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-
 // Warp-level wait for the epilogue: one lane polls, with a growing sleep
 // between polls, so 128 waiting threads do not compete with the tensor
 // core's operand reads for shared memory.  Result in every lane.
@@ -695,10 +670,6 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
-#ifdef VTNK_TC_L2HINTS
-      const uint64_t pol_a = policy_evict_first();  // hidden states: read once
-      const uint64_t pol_w = policy_evict_last();   // head window: read by every tile
-#endif
       uint32_t armed[STAGES] = {};
       long long prof_wait = 0;
       int stage = 0;
@@ -725,17 +696,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * STAGE_BYTES);
 #endif
           const uint32_t lbar = map_to_rank(&S.full[stage], 0);
-#ifdef VTNK_TC_L2HINTS
-          tma_load_2d_pair_hint(st, &tmA, lbar, kb * BK, arow, pol_a);
-#else
           tma_load_2d_pair(st, &tmA, lbar, kb * BK, arow);
-#endif
 #ifndef VTNK_TC_EXPERIMENT_NOW
-#ifdef VTNK_TC_L2HINTS
-          tma_load_2d_pair_hint(st + A_BYTES, &tmW, lbar, kb * BK, wrow, pol_w);
-#else
           tma_load_2d_pair(st + A_BYTES, &tmW, lbar, kb * BK, wrow);
-#endif
 #endif
           ++armed[stage];
           if (++stage == STAGES) {
