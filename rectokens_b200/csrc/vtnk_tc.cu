@@ -43,7 +43,18 @@ __device__ unsigned long long g_prof[8];
 #define PROF_T0(name) const long long name = clock64()
 #define PROF_ACC(acc, t0) acc += clock64() - (t0)
 #define PROF_FLUSH(i, acc) atomicAdd(&g_prof[i], static_cast<unsigned long long>(acc))
+// Per-CTA %globaltimer stamps of one launch's first tile (tuning builds).
+__device__ unsigned long long g_trace[512][16];
+#define TRACE(i)                                                                  \
+  do {                                                                            \
+    if (blockIdx.x < 512) {                                                       \
+      unsigned long long t_;                                                      \
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                     \
+      g_trace[blockIdx.x][i] = t_;                                                \
+    }                                                                             \
+  } while (0)
 #else
+#define TRACE(i)
 #define PROF_T0(name)
 #define PROF_ACC(acc, t0)
 #define PROF_FLUSH(i, acc)
@@ -69,17 +80,23 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 8;  // two per TMEM lane group, splitting the 256 columns
 constexpr int MAX_NC = 32;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
-constexpr int TMEM_COLS = 2 * BN;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
 
-struct Shared {
-  uint8_t ring[STAGES][STAGE_BYTES];  // 1024-aligned stages
+// SPLIT: the split-window variant (see beam_step_kernel) with one stage
+// fewer and the buffers of its cross-CTA hand-off.
+template <bool SPLIT>
+struct SharedT {
+  static constexpr int ST = SPLIT ? STAGES - 1 : STAGES;
+  uint8_t ring[ST][STAGE_BYTES];  // 1024-aligned stages
   float chunk_x[EPI_WARPS][32][32];    // epilogue: one 32-column chunk per warp, [col][lane]
   float merge[4][MAX_NC + MAX_NC / 4 + 2][32];  // upper-half -> lower-half partial results:
                                                 // NC values, NC byte-packed columns, max, sum
+  float xmerge[SPLIT ? 4 : 1][MAX_NC + MAX_NC / 4 + 2][32];  // split: window half 1 -> half 0
   float bias[BN];
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[ST];
+  uint64_t empty[ST];
+  uint64_t xmerge_full[4];
+  uint64_t xmerge_empty[4];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t merge_full[4];
@@ -90,7 +107,12 @@ struct Shared {
   int abort;
   int sk_last;  // epilogue: this CTA finishes the current split tile
 };
-constexpr size_t SMEM_BYTES = sizeof(Shared) + 1024;
+template <bool SPLIT>
+constexpr size_t smem_bytes() {
+  return sizeof(SharedT<SPLIT>) + 1024;
+}
+static_assert(smem_bytes<false>() <= 232448 && smem_bytes<true>() <= 232448,
+              "shared memory above the 227 KB per-CTA limit");
 
 struct Params {
   int64_t rows, H;
@@ -270,6 +292,53 @@ __device__ __forceinline__ bool warp_wait_phase(uint64_t* b, uint32_t parity, vo
   return ok != 0;
 }
 
+// One arrival for the whole warp on a CTA-local barrier, ordered after every
+// lane's earlier shared-memory accesses (__syncwarp orders them before lane
+// 0's release).  One arrival instead of 32: arrivals on one barrier are
+// serialised.
+__device__ __forceinline__ void warp_arrive(uint64_t* b) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(b);
+}
+// The same on a barrier of another CTA of the cluster; every lane first
+// fences its own (remote) stores at cluster scope.
+__device__ __forceinline__ void warp_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("fence.acq_rel.cluster;" ::: "memory");
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(cluster_addr);
+}
+
+// warp_wait_phase for a barrier that the other CTA of the cluster arrives on
+// (cluster-scope acquire).
+__device__ __forceinline__ bool warp_wait_phase_cluster(uint64_t* b, uint32_t parity,
+                                                        volatile int* abort, int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    if (!mbar_try_wait_cluster(b, parity)) {
+      const uint64_t t0 = gtimer();
+      uint32_t ns = 32;
+      for (;;) {
+        __nanosleep(ns);
+        if (mbar_try_wait_cluster(b, parity)) break;
+        if (ns < 512) ns <<= 1;
+        if (*abort) {
+          ok = 0;
+          break;
+        }
+        if (gtimer() - t0 > WAIT_LIMIT_NS) {
+          *abort = 1;
+          atomicCAS(&g_tc_status, 0, code);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  if (ok) mbar_try_wait_cluster(b, parity);  // every lane acquires
+  return ok != 0;
+}
+
 // Drain wait at teardown: bounded, never sets abort.
 __device__ __forceinline__ void drain_phase(uint64_t* b, uint32_t parity) {
   const uint64_t t0 = gtimer();
@@ -298,8 +367,13 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(const void* smem) {
 }
 // Instruction descriptor: kind::f16, A = B = bf16, D = fp32, both K-major,
 // N = 256, M = 256 (a cta_group::2 pair, 128 rows per CTA).
-constexpr uint32_t IDESC =
-    (1u << 4) | (1u << 7) | (1u << 10) | ((BN >> 3) << 17) | ((PAIR_M >> 4) << 24);
+constexpr uint32_t idesc(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+constexpr uint32_t IDESC = idesc(PAIR_M, BN);
+// Split-window variant: one CTA, M = 128 rows, N = 128 columns (half the window).
+constexpr uint32_t IDESC_SPLIT = idesc(BM, BN / 2);
 
 __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t da, uint64_t db,
                                           uint32_t accumulate) {
@@ -309,6 +383,27 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t da, uint64_t
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(da), "l"(db), "r"(IDESC), "r"(accumulate)
       : "memory");
+}
+__device__ __forceinline__ void umma_bf16_cta(uint32_t d_tmem, uint64_t da, uint64_t db,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(da), "l"(db), "r"(IDESC_SPLIT), "r"(accumulate)
+      : "memory");
+}
+// Arrive on this CTA's barrier `bar` once all previously issued MMAs of this
+// thread are complete.
+__device__ __forceinline__ void umma_commit_cta(uint64_t* bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+          su32(bar))
+      : "memory");
+}
+// Store to the same shared-memory offset in another CTA of the cluster.
+__device__ __forceinline__ void st_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
 }
 // Arrive on barrier `bar` (same offset) in both CTAs of the pair once all
 // previously issued MMAs of this thread are complete.
@@ -614,10 +709,22 @@ __device__ void row_scalar(const Params& p, int64_t row, int64_t start, int coun
 }
 
 // SAMPLE: Gumbel-max sampling (NC == 1) instead of top-n + log-sum-exp.
-template <int NC, bool SAMPLE>
+// SPLIT: the split-window variant for launches with fewer 256-row tiles than
+// SM pairs.  Both CTAs of a cluster take the same 128 rows; CTA r multiplies
+// them by window columns [128 r, 128 r + 128) with its own cta_group::1 MMAs
+// (M = 128, N = 128), so a tile's MMA chain and each epilogue warp's columns
+// are half as long.  CTA 1 hands its partial result to CTA 0 through
+// distributed shared memory; CTA 0 writes the outputs.
+template <int NC, bool SAMPLE, bool SPLIT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                  const Params p) {
+  using Shared = SharedT<SPLIT>;
+  constexpr int ST = Shared::ST;
+  constexpr int64_t TILE_ROWS = SPLIT ? BM : PAIR_M;
+  constexpr int BUF_COLS = SPLIT ? BN / 2 : BN;  // TMEM columns of one accumulator
+  constexpr uint32_t ALLOC_COLS = 2 * BUF_COLS;
+  constexpr int NCW = SPLIT ? BN / 128 : BN / 64;  // 32-column chunks per epilogue warp
   extern __shared__ uint8_t smem_raw[];
   Shared& S = *reinterpret_cast<Shared*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                          ~static_cast<uintptr_t>(1023));
@@ -628,19 +735,24 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int64_t n_pairs = gridDim.x >> 1;
   const int kblocks = static_cast<int>((p.H + BK - 1) / BK);
   volatile int* abort = &S.abort;
+  if (threadIdx.x == 0) TRACE(0);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < ST; ++s) {
       mbar_init(&S.full[s], 1);   // leader: its expect_tx arrival + both CTAs' bytes
       mbar_init(&S.empty[s], 1);  // both: the leader's MMA commit
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&S.tfull[b], 1);                // both: the leader's MMA commit
-      mbar_init(&S.tempty[b], 2 * EPI_WARPS);   // leader: every epilogue warp of the pair
+      mbar_init(&S.tfull[b], 1);  // both: the leader's MMA commit
+      // pair: every epilogue warp of both CTAs arrives on the leader's; split: own warps
+      mbar_init(&S.tempty[b], SPLIT ? EPI_WARPS : 2 * EPI_WARPS);
     }
     for (int g = 0; g < 4; ++g) {
-      mbar_init(&S.merge_full[g], 32);
-      mbar_init(&S.merge_empty[g], 32);
+      // one arrival per warp (lane 0 after the warp's writes; see warp_arrive)
+      mbar_init(&S.merge_full[g], 1);
+      mbar_init(&S.merge_empty[g], 1);
+      mbar_init(&S.xmerge_full[g], 1);
+      mbar_init(&S.xmerge_empty[g], 1);
     }
     mbar_init(&S.mma_done, 1);
     mbar_init(&S.epi_sync, EPI_WARPS);
@@ -648,11 +760,19 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {  // same warp and same smem offset in both CTAs
-    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     su32(&S.tmem_base)),
-                 "r"(TMEM_COLS)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    if constexpr (SPLIT) {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       su32(&S.tmem_base)),
+                   "r"(ALLOC_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       su32(&S.tmem_base)),
+                   "r"(ALLOC_COLS)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
   }
   for (int i = threadIdx.x; i < BN; i += THREADS) {
     const int64_t col = p.window_lo + i;
@@ -664,14 +784,15 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   cluster_sync();  // both CTAs' barriers exist before any cross-CTA signal
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
+  if (threadIdx.x == 0) TRACE(1);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
     if (lane == 0) {
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
-      uint32_t armed[STAGES] = {};
-      long long prof_wait = 0;
+      uint32_t armed[ST] = {};
+      [[maybe_unused]] long long prof_wait = 0;
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -680,7 +801,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       seg.init(p, static_cast<int>(pair));
       Seg sg;
       while (ok && seg.next(p, kblocks, n_pairs, sg)) {
-        const int arow = static_cast<int>(sg.tile * PAIR_M) + static_cast<int>(rank) * BM;
+        const int arow = static_cast<int>(sg.tile * TILE_ROWS) + (SPLIT ? 0 : static_cast<int>(rank) * BM);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           PROF_T0(t_w);
           if (!wait_phase(&S.empty[stage], phase ^ 1, abort, 1)) {
@@ -689,19 +810,26 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
           PROF_ACC(prof_wait, t_w);
           uint8_t* st = S.ring[stage];
+          if constexpr (SPLIT) {  // this CTA's own barrier and bytes
+            mbar_expect_tx(&S.full[stage], STAGE_BYTES);
+            tma_load_2d(st, &tmA, &S.full[stage], kb * BK, arow);
+            tma_load_2d(st + A_BYTES, &tmW, &S.full[stage], kb * BK, wrow);
+          } else {
 #ifdef VTNK_TC_EXPERIMENT_NOW
-          // tuning experiment only (outputs meaningless): A copies alone
-          if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * A_BYTES);
+            // tuning experiment only (outputs meaningless): A copies alone
+            if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * A_BYTES);
 #else
-          if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * STAGE_BYTES);
+            if (rank == 0) mbar_expect_tx(&S.full[stage], 2 * STAGE_BYTES);
 #endif
-          const uint32_t lbar = map_to_rank(&S.full[stage], 0);
-          tma_load_2d_pair(st, &tmA, lbar, kb * BK, arow);
+            const uint32_t lbar = map_to_rank(&S.full[stage], 0);
+            tma_load_2d_pair(st, &tmA, lbar, kb * BK, arow);
 #ifndef VTNK_TC_EXPERIMENT_NOW
-          tma_load_2d_pair(st + A_BYTES, &tmW, lbar, kb * BK, wrow);
+            tma_load_2d_pair(st + A_BYTES, &tmW, lbar, kb * BK, wrow);
 #endif
+          }
+          if (armed[stage] == 0 && stage == 0) TRACE(2);
           ++armed[stage];
-          if (++stage == STAGES) {
+          if (++stage == ST) {
             stage = 0;
             phase ^= 1;
           }
@@ -709,29 +837,31 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       }
       // the leader's barriers count both CTAs' copies: it waits for any still in
       // flight; the peer stays resident until the teardown cluster barrier
-      if (rank == 0)
-        for (int s = 0; s < STAGES; ++s)
+      if (SPLIT || rank == 0)
+        for (int s = 0; s < ST; ++s)
           if (armed[s]) drain_phase(&S.full[s], (armed[s] - 1) & 1);
       PROF_FLUSH(0, prof_wait);
     }
   } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer (leader)
-    if (lane == 0 && rank == 0) {
+    // ------------------------------------------- MMA issuer (pair: leader; split: each CTA)
+    if (lane == 0 && (SPLIT || rank == 0)) {
       int stage = 0;
       uint32_t phase = 0;
       uint32_t it = 0;
       bool ok = true;
-      long long prof_full = 0, prof_tempty = 0;
+      [[maybe_unused]] long long prof_full = 0, prof_tempty = 0;
       SegIter seg;
       seg.init(p, static_cast<int>(pair));
       Seg sg;
       for (; ok && seg.next(p, kblocks, n_pairs, sg); ++it) {
         const uint32_t buf = it & 1;
         PROF_T0(t_e);
-        if (!wait_phase_cluster(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)) break;
+        if (SPLIT ? !wait_phase(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)
+                  : !wait_phase_cluster(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2))
+          break;
         PROF_ACC(prof_tempty, t_e);
         tc_fence_after();
-        const uint32_t d = tmem + buf * BN;
+        const uint32_t d = tmem + buf * BUF_COLS;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           PROF_T0(t_f);
           if (!wait_phase(&S.full[stage], phase, abort, 3)) {
@@ -739,21 +869,39 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             break;
           }
           PROF_ACC(prof_full, t_f);
+          if (it == 0 && kb == sg.kb0) TRACE(3);
           tc_fence_after();
           const uint64_t da = umma_desc_sw128(S.ring[stage]);
           const uint64_t db = umma_desc_sw128(S.ring[stage] + A_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)  // +32 B per K=16 step inside the swizzle atom
-            umma_bf16(d, da + 2 * k, db + 2 * k, (kb != sg.kb0 || k != 0) ? 1u : 0u);
-          umma_commit_pair(&S.empty[stage]);
-          if (++stage == STAGES) {
+          for (int k = 0; k < BK / 16; ++k) {  // +32 B per K=16 step inside the swizzle atom
+            const uint32_t acc = (kb != sg.kb0 || k != 0) ? 1u : 0u;
+            if constexpr (SPLIT)
+              umma_bf16_cta(d, da + 2 * k, db + 2 * k, acc);
+            else
+              umma_bf16(d, da + 2 * k, db + 2 * k, acc);
+          }
+          if constexpr (SPLIT)
+            umma_commit_cta(&S.empty[stage]);
+          else
+            umma_commit_pair(&S.empty[stage]);
+          if (++stage == ST) {
             stage = 0;
             phase ^= 1;
           }
         }
-        if (ok) umma_commit_pair(&S.tfull[buf]);
+        if (ok) {
+          if constexpr (SPLIT)
+            umma_commit_cta(&S.tfull[buf]);
+          else
+            umma_commit_pair(&S.tfull[buf]);
+        }
       }
-      umma_commit_pair(&S.mma_done);
+      TRACE(4);
+      if constexpr (SPLIT)
+        umma_commit_cta(&S.mma_done);
+      else
+        umma_commit_pair(&S.mma_done);
       drain_phase(&S.mma_done, 0);
       PROF_FLUSH(1, prof_full);
       PROF_FLUSH(2, prof_tempty);
@@ -761,12 +909,26 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   } else {
     // ---------------------------------------------------------------- epilogue
     const int lg = warp & 3;             // TMEM lane group this warp may access
-    const int half = (warp - 2) >> 2;    // 0: columns 0..127 (+ merge, outputs); 1: 128..255
+    // pair: half 0 = columns 0..127 (+ merge, outputs), half 1 = 128..255;
+    // split: the same two halves of this CTA's 128 columns
+    const int half = (warp - 2) >> 2;
     const int r_local = lg * 32 + lane;  // row within the tile == TMEM lane
     uint32_t it = 0;
-    long long pe_pro = 0, pe_wait = 0, pe_tmem = 0, pe_out = 0, pe_ld = 0;
+    [[maybe_unused]] long long pe_pro = 0, pe_wait = 0, pe_tmem = 0, pe_out = 0, pe_ld = 0;
     const uint32_t tempty_leader[2] = {map_to_rank(&S.tempty[0], 0), map_to_rank(&S.tempty[1], 0)};
+    // Give the accumulator back to the MMA issuer (every lane is done reading it).
+    auto release_acc = [&](uint32_t b) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if constexpr (SPLIT)
+          mbar_arrive(&S.tempty[b]);
+        else
+          mbar_arrive_cluster(tempty_leader[b]);  // the leader's MMA may reuse it
+      }
+    };
     uint32_t mit = 0;  // hand-offs between the two column halves so far
+    uint32_t xit = 0;  // split: hand-offs from CTA 1 to CTA 0 so far
     uint32_t eb = 0;   // epi_sync phases so far
     // All epilogue warps of the CTA meet (bounded wait; false on abort).
     auto epi_sync = [&]() {
@@ -783,7 +945,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     for (; seg.next(p, kblocks, n_pairs, sg); ++it) {
       const int64_t tile = sg.tile;
       PROF_T0(t_pro);
-      const int64_t row = tile * PAIR_M + static_cast<int64_t>(rank) * BM + r_local;
+      const int64_t row = tile * TILE_ROWS + (SPLIT ? 0 : static_cast<int64_t>(rank) * BM) + r_local;
       const bool live = row < p.rows;
       // The row's children as a 256-bit mask over the window, read from the
       // depth's child index (two 16-byte loads).  A row whose node is outside
@@ -819,52 +981,55 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // every lane observes the completed phase before touching TMEM
       mbar_try_wait(&S.tfull[buf], (it >> 1) & 1);
       tc_fence_after();
+      if (warp == 2 && lane == 0 && it == 0) TRACE(5);
       PROF_ACC(pe_wait, t_wt);
       PROF_T0(t_tm);
 #ifdef VTNK_TC_EXPERIMENT_NOEPI
       // tuning experiment only (no outputs written): release the accumulator at once
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);
+      release_acc(buf);
       continue;
 #endif
 
-      const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BN;
+      // TMEM address of window chunk c is taddr + 32 c (split: this CTA's
+      // chunks 4 r .. 4 r + 3 map to its buffer's columns 0..127).
+      const uint32_t taddr = tmem + (static_cast<uint32_t>(lg * 32) << 16) + buf * BUF_COLS -
+                             (SPLIT ? rank * (BN / 2) : 0u);
       const bool has_bias = p.bias != nullptr;
-      const int c0 = half * (BN / 64);  // this warp's first 32-column chunk
+      // this warp's first 32-column chunk of the window
+      const int c0 = SPLIT ? static_cast<int>(rank) * (BN / 64) + half * NCW : half * NCW;
       // A segment that covers part of a tile stores its raw accumulator
       // (this warp's 32 rows x 128 columns) as an fp32 partial and counts
       // its k-blocks.  The contributor that completes the tile replaces its
       // TMEM buffer by the sum of all partials and runs the epilogue; the
       // others free the buffer.
-      if (sg.kb0 != 0 || sg.kb1 != kblocks) {
-        // This CTA's raw accumulator of the segment (coalesced fp32 partial).
+      if constexpr (!SPLIT) {  // stream-K (whole tiles only in the split variant)
+        if (sg.kb0 != 0 || sg.kb1 != kblocks) {
+          // This CTA's raw accumulator of the segment (coalesced fp32 partial).
 #pragma unroll 1
-        for (int ci = 0; ci < BN / 64; ++ci) {
-          uint32_t v[32];
-          __syncwarp();
-          tmem_ld32(taddr + (c0 + ci) * 32, v);
+          for (int ci = 0; ci < BN / 64; ++ci) {
+            uint32_t v[32];
+            __syncwarp();
+            tmem_ld32(taddr + (c0 + ci) * 32, v);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            __stcg(part_at(p, pair, sg.slot, rank, c0 + ci, q, r_local),
-                   make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
-                               __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])));
+            for (int q = 0; q < 8; ++q)
+              __stcg(part_at(p, pair, sg.slot, rank, c0 + ci, q, r_local),
+                     make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                 __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3])));
+          }
+          __threadfence();
+          if (!epi_sync()) break;
+          if (warp == 2 && lane == 0)
+            S.sk_last = sk_arrive(p.sk_count + sg.sk_tile * 2 + rank, p.sk_epoch,
+                                  sg.kb1 - sg.kb0, kblocks) ? 1 : 0;
+          if (!epi_sync()) break;
+          const int finisher = *reinterpret_cast<volatile int*>(&S.sk_last);
+          if (!finisher) {
+            release_acc(buf);
+            continue;
+          }
+          __threadfence();
+          sum_partials_to_tmem(p, sg.sk_tile, kblocks, rank, r_local, c0, taddr);
         }
-        __threadfence();
-        if (!epi_sync()) break;
-        if (warp == 2 && lane == 0)
-          S.sk_last = sk_arrive(p.sk_count + sg.sk_tile * 2 + rank, p.sk_epoch,
-                                sg.kb1 - sg.kb0, kblocks) ? 1 : 0;
-        if (!epi_sync()) break;
-        const int finisher = *reinterpret_cast<volatile int*>(&S.sk_last);
-        if (!finisher) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);
-          continue;
-        }
-        __threadfence();
-        sum_partials_to_tmem(p, sg.sk_tile, kblocks, rank, r_local, c0, taddr);
       }
 
       TopN<NC> top;
@@ -882,7 +1047,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float* sx = &S.chunk_x[warp - 2][0][0];
         const uint32_t off0 = static_cast<uint32_t>(row * p.mb);
 #pragma unroll 1
-        for (int ci = 0; ci < BN / 64; ++ci) {
+        for (int ci = 0; ci < NCW; ++ci) {
           const int chunk = c0 + ci;
           uint32_t mw = 0;
 #pragma unroll
@@ -920,9 +1085,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float gm[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) gm[g] = -INFINITY;
-        float cmax[BN / 64];
+        float cmax[NCW];
 #pragma unroll
-        for (int ci = 0; ci < BN / 64; ++ci) {
+        for (int ci = 0; ci < NCW; ++ci) {
           const int chunk = c0 + ci;
           float x[32];
           load_chunk(taddr, chunk, m, has_bias, S.bias, x);
@@ -942,14 +1107,15 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             for (int i = 0; i < w; ++i) e[i] += e[i + w];
           sum += e[0];
         }
-        const float lb = nth_largest<G, NC>(gm);
+        if (warp == 2 && lane == 0 && it == 0) TRACE(8);
+      const float lb = nth_largest<G, NC>(gm);
         // Pass 2: top-n in column order over the values >= lb.  Each lane
         // inserts only its values above its current n-th best; the warp loops
         // max-over-lanes(candidates) times.  Values are read back from shared
         // memory ([col][lane]: conflict-free for any per-lane column).
         float* sx = &S.chunk_x[warp - 2][0][0];
 #pragma unroll 1
-        for (int ci = 0; ci < BN / 64; ++ci) {
+        for (int ci = 0; ci < NCW; ++ci) {
           if (!__any_sync(0xffffffffu, cmax[ci] >= lb && cmax[ci] > -INFINITY)) continue;
           const int chunk = c0 + ci;
           float x[32];
@@ -982,58 +1148,86 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
       }
       __syncwarp();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(tempty_leader[buf]);  // the leader's MMA may reuse it
+      release_acc(buf);
 
-      // The upper-half warp hands (top-n, max, sum) to the lower-half warp of
-      // the same rows through shared memory; bounded waits on both sides.
-      float (*mg)[32] = S.merge[lg];
-      if (half == 1) {
-        if (!warp_wait_phase(&S.merge_empty[lg], (mit & 1) ^ 1, abort, 5)) break;
-        mbar_try_wait(&S.merge_empty[lg], (mit & 1) ^ 1);
+      if (warp == 2 && lane == 0 && it == 0) TRACE(9);
+      // A partial result (top-n, max, sum) travels as rows of a [*][32] table
+      // (lane = row): NC values, NC byte-packed columns (window columns are
+      // < 256; 0xFF = none), max, sum.
+      auto put_list = [&](auto store) {
 #pragma unroll
-        for (int j = 0; j < NC; ++j) mg[j][lane] = top.v[j];
+        for (int j = 0; j < NC; ++j) store(j, top.v[j]);
 #pragma unroll
-        for (int j = 0; j < NC; j += 4) {  // columns < 256: four per word, 0xFF = none
+        for (int j = 0; j < NC; j += 4) {
           uint32_t w = 0;
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             if (j + q < NC) w |= static_cast<uint32_t>(top.c[j + q] & 0xFF) << (8 * q);
             else w |= 0xFFu << (8 * q);
-          mg[MAX_NC + j / 4][lane] = __uint_as_float(w);
+          store(MAX_NC + j / 4, __uint_as_float(w));
         }
-        mg[MAX_NC + MAX_NC / 4][lane] = mx;
-        mg[MAX_NC + MAX_NC / 4 + 1][lane] = sum;
-        mbar_arrive(&S.merge_full[lg]);
+        store(MAX_NC + MAX_NC / 4, mx);
+        store(MAX_NC + MAX_NC / 4 + 1, sum);
+      };
+      // Merges a table written by put_list whose columns are all higher than
+      // this warp's: inserting its sorted list after ours keeps ties on the
+      // lower column.
+      auto absorb = [&](float (*src)[32]) {
+        const float omx = src[MAX_NC + MAX_NC / 4][lane];
+        const float osum = src[MAX_NC + MAX_NC / 4 + 1][lane];
+        const float nm = fmaxf(mx, omx);
+        sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) +
+              (omx > -INFINITY ? osum * __expf(omx - nm) : 0.f);
+        mx = nm;
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+          const float y = src[j][lane];
+          const uint32_t cb = (__float_as_uint(src[MAX_NC + j / 4][lane]) >> (8 * (j & 3))) & 0xFFu;
+          const int c = (y > -INFINITY) ? static_cast<int>(cb) : -1;  // column 255 packs as 0xFF too
+          if (__any_sync(0xffffffffu, y > top.v[NC - 1])) top.insert(y, c);
+        }
+      };
+
+      // The upper-half warp hands its partial result to the lower-half warp
+      // of the same rows through shared memory; bounded waits on both sides.
+      float (*mg)[32] = S.merge[lg];
+      if (half == 1) {
+        if (!warp_wait_phase(&S.merge_empty[lg], (mit & 1) ^ 1, abort, 5)) break;
+        mbar_try_wait(&S.merge_empty[lg], (mit & 1) ^ 1);
+        put_list([&](int r, float v) { mg[r][lane] = v; });
+        warp_arrive(&S.merge_full[lg]);
         ++mit;
         PROF_ACC(pe_tmem, t_tm);
         continue;
       }
       if (!warp_wait_phase(&S.merge_full[lg], mit & 1, abort, 6)) break;
       mbar_try_wait(&S.merge_full[lg], mit & 1);
-      {
-        const float omx = mg[MAX_NC + MAX_NC / 4][lane];
-        const float osum = mg[MAX_NC + MAX_NC / 4 + 1][lane];
-        const float nm = fmaxf(mx, omx);
-        sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) +
-              (omx > -INFINITY ? osum * __expf(omx - nm) : 0.f);
-        mx = nm;
-        // the other half's columns are all higher: inserting its sorted list
-        // after ours keeps ties on the lower column
-#pragma unroll
-        for (int j = 0; j < NC; ++j) {
-          const float y = mg[j][lane];
-          const uint32_t cb = (__float_as_uint(mg[MAX_NC + j / 4][lane]) >> (8 * (j & 3))) & 0xFFu;
-          const int c = (y > -INFINITY) ? static_cast<int>(cb) : -1;  // column 255 packs as 0xFF too
-          if (__any_sync(0xffffffffu, y > top.v[NC - 1])) top.insert(y, c);
-        }
-      }
-      mbar_arrive(&S.merge_empty[lg]);
+      absorb(mg);
+      warp_arrive(&S.merge_empty[lg]);
       ++mit;
+      if (warp == 2 && lane == 0 && it == 0) TRACE(10);
+
+      if constexpr (SPLIT) {
+        // CTA 1 (window columns 128..255) hands its rows' result to CTA 0
+        // through distributed shared memory (remote stores, release/acquire
+        // at cluster scope on the barriers); CTA 0 writes the outputs.
+        if (rank == 1) {
+          if (!warp_wait_phase_cluster(&S.xmerge_empty[lg], (xit & 1) ^ 1, abort, 8)) break;
+          put_list([&](int r, float v) { st_cluster_f32(map_to_rank(&S.xmerge[lg][r][lane], 0), v); });
+          warp_arrive_cluster(map_to_rank(&S.xmerge_full[lg], 0));
+          ++xit;
+          PROF_ACC(pe_tmem, t_tm);
+          continue;
+        }
+        if (!warp_wait_phase_cluster(&S.xmerge_full[lg], xit & 1, abort, 9)) break;
+        absorb(S.xmerge[lg]);
+        warp_arrive_cluster(map_to_rank(&S.xmerge_empty[lg], 1));
+        ++xit;
+      }
 
       PROF_ACC(pe_tmem, t_tm);
       PROF_T0(t_out);
+      if (warp == 2 && lane == 0 && it == 0) TRACE(11);
       float lse = (mx > -INFINITY) ? mx + __logf(sum) : -INFINITY;
       bool by_slot = false;
       if (spill && live) {  // exact scalar recompute of this row
@@ -1041,6 +1235,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         row_scalar<NC>(p, row, start, count, top, lse, SAMPLE, temp);
         by_slot = true;
       }
+      if (warp == 2 && lane == 0 && it == 0) TRACE(12);
       if (live) {
         int pre[BN / 32];
         int acc = 0;
@@ -1083,6 +1278,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         if (p.row_lse) p.row_lse[row] = lse;
       }
+      if (warp == 2 && lane == 0 && it == 0) TRACE(6);
       PROF_ACC(pe_out, t_out);
     }
     if (lane == 0) {
@@ -1098,11 +1294,17 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // the pair's MMAs and copies are done before either CTA frees or exits
+  if (threadIdx.x == 0) TRACE(7);
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                 "r"(TMEM_COLS)
-                 : "memory");
+    if constexpr (SPLIT)
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(ALLOC_COLS)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                   "r"(ALLOC_COLS)
+                   : "memory");
   }
 }
 
@@ -1188,22 +1390,30 @@ int sm_count() {
   return n;
 }
 
-template <int NC, bool SAMPLE = false>
-int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, int pairs,
-              cudaStream_t s) {
-  auto k = beam_step_kernel<NC, SAMPLE>;
+template <int NC, bool SAMPLE, bool SPLIT>
+int launch_variant(const CUtensorMap& a, const CUtensorMap& w, const Params& p, int pairs,
+                   cudaStream_t s) {
+  auto k = beam_step_kernel<NC, SAMPLE, SPLIT>;
+  constexpr size_t smem = smem_bytes<SPLIT>();
   // The shared-memory opt-in is per kernel and device; set it once each.
   static std::atomic<uint64_t> set_on{0};  // bit d: done on device d
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !((set_on.load(std::memory_order_relaxed) >> dev) & 1)) {
     const cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               static_cast<int>(SMEM_BYTES));
+                                               static_cast<int>(smem));
     if (e != cudaSuccess) return cuda_status(e, "beam_step_tc smem attribute");
     if (dev < 64) set_on.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
-  k<<<2 * pairs, THREADS, SMEM_BYTES, s>>>(a, w, p);
+  k<<<2 * pairs, THREADS, smem, s>>>(a, w, p);
   return cuda_status(cudaGetLastError(), "beam_step_tc launch");
+}
+
+template <int NC, bool SAMPLE = false>
+int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, int pairs, bool split,
+              cudaStream_t s) {
+  return split ? launch_variant<NC, SAMPLE, true>(a, w, p, pairs, s)
+               : launch_variant<NC, SAMPLE, false>(a, w, p, pairs, s);
 }
 
 }  // namespace tc
@@ -1262,7 +1472,23 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.dp_tiles = n_tiles;
   p.sk_iters = 0;
   p.sk_pairs = 0;
-  if (t.sk_part && t.sk_count && n_tiles % max_pairs != 0) {
+  // Fewer 256-row tiles than pairs: the split-window variant (128-row tiles,
+  // two CTAs per tile with half the window each) puts up to twice as many
+  // SMs to work.  Measured on B200 it shortens sampling launches (cfg4
+  // 0.19 -> 0.15 ms per search) and leaves top-n launches unchanged, whose
+  // one-tile time is bound by operand delivery (~100 GB/s per SM) and the
+  // cross-CTA hand-off; so by default it serves sampling only.
+  // VTNK_SPLIT=1: top-n too; VTNK_SPLIT=0: never.
+  static const int split_mode = [] {
+    const char* e = getenv("VTNK_SPLIT");
+    return (e && e[0] == '0') ? 0 : (e && e[0] == '1') ? 2 : 1;
+  }();
+  const bool split = n_tiles < max_pairs && (split_mode == 2 || (split_mode == 1 && t.sample));
+  if (split) {
+    const int64_t tiles128 = (t.rows + BM - 1) / BM;
+    p.dp_tiles = tiles128;
+    pairs = tiles128 < max_pairs ? tiles128 : max_pairs;
+  } else if (t.sk_part && t.sk_count && n_tiles % max_pairs != 0) {
     const int64_t rounds = n_tiles / max_pairs;
     const int64_t dp = rounds > 0 ? (rounds - 1) * max_pairs : 0;
     const int64_t iters = (n_tiles - dp) * kblocks;
@@ -1286,18 +1512,18 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
     set_error("cuTensorMapEncodeTiled failed");
     return VTNK_ERR_CUDA;
   }
-  if (t.sample) return t.n_cand == 1 ? launch_nc<1, true>(ma, mw, p, np, s) : VTNK_ERR_UNSUPPORTED;
+  if (t.sample) return t.n_cand == 1 ? launch_nc<1, true>(ma, mw, p, np, split, s) : VTNK_ERR_UNSUPPORTED;
   switch (t.n_cand) {  // exact widths for the common beam sizes
-    case 1: return launch_nc<1>(ma, mw, p, np, s);
-    case 5: return launch_nc<5>(ma, mw, p, np, s);
-    case 10: return launch_nc<10>(ma, mw, p, np, s);
-    case 20: return launch_nc<20>(ma, mw, p, np, s);
+    case 1: return launch_nc<1>(ma, mw, p, np, split, s);
+    case 5: return launch_nc<5>(ma, mw, p, np, split, s);
+    case 10: return launch_nc<10>(ma, mw, p, np, split, s);
+    case 20: return launch_nc<20>(ma, mw, p, np, split, s);
     default: break;
   }
-  if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, np, s);
-  if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, np, s);
-  if (t.n_cand <= 16) return launch_nc<16>(ma, mw, p, np, s);
-  return launch_nc<32>(ma, mw, p, np, s);
+  if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, np, split, s);
+  if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, np, split, s);
+  if (t.n_cand <= 16) return launch_nc<16>(ma, mw, p, np, split, s);
+  return launch_nc<32>(ma, mw, p, np, split, s);
 }
 
 int launch_build_child_index(const Csr& csr, uint32_t* masks, int64_t node_lo, int64_t node_hi,
@@ -1328,6 +1554,12 @@ int read_tc_status(int* out, bool reset) {
 
 #ifdef VTNK_TC_PROFILE
 // Tuning builds only: copy (and optionally clear) the phase timers.
+extern "C" int vtnk_tc_trace(unsigned long long* out) {
+  cudaDeviceSynchronize();
+  cudaMemcpyFromSymbol(out, vtnk::g_trace, sizeof(unsigned long long) * 512 * 16);
+  return 0;
+}
+
 extern "C" int vtnk_tc_profile(unsigned long long* out, int reset) {
   cudaDeviceSynchronize();
   cudaMemcpyFromSymbol(out, vtnk::g_prof, sizeof(unsigned long long) * 8);

@@ -334,20 +334,26 @@ print("ok")
 """
 
 
-@pytest.mark.parametrize("stream_k", ["0", "1"])
-def test_tile_kernel_deterministic_and_split_tiles(stream_k, cuda_ok):
-    """Repeated launches give bit-identical results, with whole-tile rounds
-    and with the opt-in stream-K schedule (VTNK_STREAMK=1: tiles split
-    across SM pairs, fp32 partials summed by the last contributor in pair
-    order), and both match the row kernel.  Runs in a child process because
-    the schedule is chosen when the library loads."""
+@pytest.mark.parametrize("schedule", [
+    {},                                      # default: 2-SM pair tiles for top-n launches
+    {"VTNK_SPLIT": "1"},                     # split-window tiles for small top-n launches too
+    {"VTNK_SPLIT": "0", "VTNK_STREAMK": "1"},  # pair tiles + stream-K split tiles
+], ids=["pair", "split", "stream_k"])
+def test_tile_kernel_schedules(schedule, cuda_ok):
+    """Every tile schedule gives bit-identical results on repeated launches
+    and matches the row kernel: the split-window variant (two CTAs per
+    128-row tile with half the window each, hand-off through distributed
+    shared memory), whole 2-SM pair tiles, and the opt-in stream-K schedule
+    (fp32 partials summed by the last contributor in pair order).  Runs in a
+    child process because the schedule is chosen when the library loads."""
     import os
     import subprocess
     import sys
     from pathlib import Path
 
     root = Path(__file__).resolve().parents[1]
-    env = dict(os.environ, VTNK_STREAMK=stream_k, PYTHONPATH=str(root))
+    env = {k: v for k, v in os.environ.items() if k not in ("VTNK_SPLIT", "VTNK_STREAMK")}
+    env.update(schedule, PYTHONPATH=str(root))
     r = subprocess.run([sys.executable, "-c", _SPLIT_CHECK], cwd=root, env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
