@@ -122,6 +122,11 @@ typedef struct {
   int64_t node_hi;
   int64_t window_lo;
   int64_t window_n;       /* 1..256 */
+  uint32_t* flags;        /* optional, one word written by vtnk_build_child_index: bit 0 set
+                             when every child of every node in range has node id = its
+                             edge index + 1 (BFS numbering, as the reference's builders
+                             produce); the beam step then computes child node ids
+                             instead of reading vals.  NULL: always read vals. */
 } vtnk_child_index_t;
 
 /* The _topk entry point with the depth's child index: the tcgen05 tile
@@ -151,8 +156,9 @@ int vtnk_fused_linear_constrained_node_transition_sampling_ix(
     const vtnk_child_index_t* index, int64_t* next_node, int64_t* valid_idxs, float* sample,
     int64_t* sample_node, void* stream);
 
-/* Builds index->masks (caller memory, (node_hi - node_lo) * 32 bytes) for
- * the nodes and window described by `index` (no reference counterpart). */
+/* Builds index->masks (caller memory, (node_hi - node_lo) * 32 bytes) and,
+ * when index->flags is given, its flag word, for the nodes and window
+ * described by `index` (no reference counterpart). */
 int vtnk_build_child_index(const vtnk_csr_t* csr, const vtnk_child_index_t* index,
                            void* stream);
 

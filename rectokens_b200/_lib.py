@@ -51,7 +51,7 @@ class Linear(ctypes.Structure):
 
 class ChildIndex(ctypes.Structure):
     _fields_ = [("masks", c_void_p), ("node_lo", c_int64), ("node_hi", c_int64),
-                ("window_lo", c_int64), ("window_n", c_int64)]
+                ("window_lo", c_int64), ("window_n", c_int64), ("flags", c_void_p)]
 
 
 class Search(ctypes.Structure):

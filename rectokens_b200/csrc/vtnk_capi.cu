@@ -183,6 +183,7 @@ int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t*
     t.window_lo = index->window_lo;
     t.window_n = static_cast<int>(index->window_n);
     t.masks = index->masks;
+    t.flags = index->flags;
     t.idx_lo = index->node_lo;
     t.idx_hi = index->node_hi;
     t.bias = lin->bias;
@@ -391,7 +392,7 @@ int vtnk_build_child_index(const vtnk_csr_t* csr, const vtnk_child_index_t* inde
   VTNK_REQUIRE((reinterpret_cast<uintptr_t>(index->masks) & 15) == 0,
                "masks must be 16-byte aligned");
   return launch_build_child_index(make_csr(*csr), const_cast<uint32_t*>(index->masks),
-                                  index->node_lo, index->node_hi, index->window_lo,
+                                  index->flags, index->node_lo, index->node_hi, index->window_lo,
                                   static_cast<int>(index->window_n), as_stream(stream));
 }
 

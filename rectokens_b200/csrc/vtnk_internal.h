@@ -59,6 +59,7 @@ struct TcArgs {
   int64_t window_lo;        // first token of the column window
   int window_n;             // <= 256
   const uint32_t* masks;    // child-bitmask index [idx_hi - idx_lo, 8]
+  const uint32_t* flags;    // index flag word or nullptr (bit 0: node id = edge index + 1)
   int64_t idx_lo, idx_hi;
   const void* bias;         // bf16 [N] or nullptr
   const int64_t* cur_node;  // nullptr: root
@@ -111,8 +112,8 @@ int launch_tables(int64_t rows, const int64_t* cur_node, const Csr& csr, int64_t
 // fit the tile kernel; the caller then uses the row kernel.
 int launch_beam_step_tc(const TcArgs& p, cudaStream_t s);
 bool tc_enabled();
-int launch_build_child_index(const Csr& csr, uint32_t* masks, int64_t node_lo, int64_t node_hi,
-                             int64_t window_lo, int window_n, cudaStream_t s);
+int launch_build_child_index(const Csr& csr, uint32_t* masks, uint32_t* flags, int64_t node_lo,
+                             int64_t node_hi, int64_t window_lo, int window_n, cudaStream_t s);
 // Reads (and optionally clears) the tile kernel's device status word.
 int read_tc_status(int* out, bool reset);
 

@@ -123,6 +123,7 @@ struct Params {
   int window_n;
   int n_cand;
   const uint32_t* masks;
+  const uint32_t* flags;  // index flag word or nullptr (bit 0: child node id = edge index + 1)
   int64_t idx_lo, idx_hi;
   const __nv_bfloat16* a;
   int64_t a_stride;
@@ -929,6 +930,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     };
     uint32_t mit = 0;  // hand-offs between the two column halves so far
     uint32_t xit = 0;  // split: hand-offs from CTA 1 to CTA 0 so far
+    const bool edge_ids = p.flags != nullptr && (__ldg(p.flags) & 1u) != 0u;
     uint32_t eb = 0;   // epi_sync phases so far
     // All epilogue warps of the CTA meet (bounded wait; false on abort).
     auto epi_sync = [&]() {
@@ -1268,7 +1270,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
               slot = base + __popc(word & ((1u << (c & 31)) - 1u));
               tok = p.window_lo + c;
             }
-            node = __ldg(p.csr.vals + start + slot);
+            // BFS-numbered depth (checked when the index was built): the child's
+            // node id is its edge index + 1, no random read of vals
+            node = (edge_ids && !by_slot) ? start + slot + 1 : __ldg(p.csr.vals + start + slot);
             lv = top.v[j];
           }
           if (p.cand_tok) p.cand_tok[o + j] = tok;
@@ -1310,7 +1314,10 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 
 // Child-bitmask index: one warp per node.  Bits for children inside the
 // window; an all-zero mask when a child is outside it or out of order.
-__global__ void build_index_kernel(const Csr csr, uint32_t* __restrict__ masks, int64_t node_lo,
+// `flags` (optional, preset to bit 0 = 1 by the host): bit 0 is cleared when
+// a child's node id is not its edge index + 1.
+__global__ void build_index_kernel(const Csr csr, uint32_t* __restrict__ masks,
+                                   uint32_t* __restrict__ flags, int64_t node_lo,
                                    int64_t node_hi, int64_t window_lo, int window_n) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -1324,6 +1331,7 @@ __global__ void build_index_kernel(const Csr csr, uint32_t* __restrict__ masks, 
 #pragma unroll
     for (int i = 0; i < BN / 32; ++i) word[i] = 0u;
     int bad = 0;
+    int not_bfs = 0;
     int64_t carry = INT64_MIN;
     for (int j0 = 0; j0 < count; j0 += 32) {
       const int j = j0 + lane;
@@ -1333,6 +1341,7 @@ __global__ void build_index_kernel(const Csr csr, uint32_t* __restrict__ masks, 
       if (lane == 0) tp = carry;
       carry = __shfl_sync(0xffffffffu, t, 31);
       const bool inwin = has && t >= 0 && t < window_n;
+      if (has && __ldg(csr.vals + start + j) != start + j + 1) not_bfs = 1;
       if (has && (!inwin || t <= tp)) bad = 1;
 #pragma unroll
       for (int i = 0; i < BN / 32; ++i) {
@@ -1341,6 +1350,7 @@ __global__ void build_index_kernel(const Csr csr, uint32_t* __restrict__ masks, 
       }
     }
     bad = __any_sync(0xffffffffu, bad);
+    if (flags && __any_sync(0xffffffffu, not_bfs) && lane == 0) atomicAnd(flags, ~1u);
     if (lane < BN / 32) {
       uint32_t w = 0;
 #pragma unroll
@@ -1446,6 +1456,7 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.window_n = t.window_n;
   p.n_cand = t.n_cand;
   p.masks = t.masks;
+  p.flags = t.flags;
   p.idx_lo = t.idx_lo;
   p.idx_hi = t.idx_hi;
   p.a = static_cast<const __nv_bfloat16*>(t.a);
@@ -1526,14 +1537,18 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   return launch_nc<32>(ma, mw, p, np, split, s);
 }
 
-int launch_build_child_index(const Csr& csr, uint32_t* masks, int64_t node_lo, int64_t node_hi,
-                             int64_t window_lo, int window_n, cudaStream_t s) {
+int launch_build_child_index(const Csr& csr, uint32_t* masks, uint32_t* flags, int64_t node_lo,
+                             int64_t node_hi, int64_t window_lo, int window_n, cudaStream_t s) {
+  if (flags) {  // bit 0 set (bytes 0x01), cleared by the kernel on the first violation
+    const cudaError_t e = cudaMemsetAsync(flags, 1, sizeof(uint32_t), s);
+    if (e != cudaSuccess) return cuda_status(e, "child index flags");
+  }
   if (node_hi <= node_lo) return VTNK_OK;
   const int64_t warps = node_hi - node_lo;
   int64_t blocks = (warps + 7) / 8;
   if (blocks > 148 * 32) blocks = 148 * 32;
-  tc::build_index_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(csr, masks, node_lo, node_hi,
-                                                                  window_lo, window_n);
+  tc::build_index_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(csr, masks, flags, node_lo,
+                                                                  node_hi, window_lo, window_n);
   return cuda_status(cudaGetLastError(), "build_index_kernel launch");
 }
 

@@ -113,12 +113,16 @@ def child_index(trie: CompactCSRTrie, depth: int):
     if not 1 <= d.window_n <= 256 or trie.row_ptrs.device.type != "cuda":
         idx[depth] = (None, None)
         return None
-    masks = torch.empty((max(1, d.node_hi - d.node_lo), 8), dtype=torch.int32,
-                        device=trie.row_ptrs.device)
-    ci = L.ChildIndex(masks.data_ptr(), d.node_lo, d.node_hi, d.window_lo, d.window_n)
+    # one allocation: the masks, then one row whose first word is the flag word
+    # (bit 0: the depth's children are BFS-numbered, node id = edge index + 1)
+    n = max(1, d.node_hi - d.node_lo)
+    buf = torch.empty((n + 1, 8), dtype=torch.int32, device=trie.row_ptrs.device)
+    masks = buf[:n]
+    ci = L.ChildIndex(buf.data_ptr(), d.node_lo, d.node_hi, d.window_lo, d.window_n,
+                      buf[n].data_ptr())
     csr = L.csr_struct(trie.row_ptrs, trie.stacked_cols_vals)
     L.check(L.lib().vtnk_build_child_index(csr, ci, L.stream_of(masks.device)))
-    idx[depth] = (ci, masks)
+    idx[depth] = (ci, masks, buf)
     return ci
 
 

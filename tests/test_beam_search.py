@@ -357,3 +357,33 @@ def test_tile_kernel_schedules(schedule, cuda_ok):
     r = subprocess.run([sys.executable, "-c", _SPLIT_CHECK], cwd=root, env=env,
                        capture_output=True, text=True, timeout=600)
     assert r.returncode == 0 and r.stdout.strip().endswith("ok"), r.stdout + r.stderr
+
+
+def test_child_index_bfs_flag(cuda_ok):
+    """The index records whether a depth's child node ids are BFS edge
+    numbers (id = edge index + 1, as the reference's builders number them);
+    the tile kernel then computes node ids instead of reading them, and reads
+    them for any other numbering -- same outputs as the row kernel both ways."""
+    from rectokens_b200.decoding.beam_search import _cache_slot, child_index
+
+    w = S.WORKLOADS["cfg2"]
+    dw = WL.make_device_workload(w, DEV)
+    h = dw.hidden[1][:600]
+    cur = torch.arange(600, device=DEV) % 200 + 1       # depth-1 nodes
+    child_index(dw.trie, 1)
+    flag = _cache_slot(dw.trie)["index"][1][2][-1, 0].item()
+    assert flag & 1 == 1
+    got = beam_step(h, dw.weight, dw.trie, 1, cur, 10)
+    assert _compare_steps(got, beam_step(h, dw.weight, dw.trie, 1, cur, 10, index=None)) > 0.99
+    # the same trie with depth-2 node ids renumbered (ids + 7): still a valid
+    # table for this level's outputs, but not BFS edge numbers
+    cv = dw.trie.stacked_cols_vals.clone()
+    cv[1, :-1] += 7
+    odd = dw.trie._replace(stacked_cols_vals=cv)
+    child_index(odd, 1)
+    assert _cache_slot(odd)["index"][1][2][-1, 0].item() & 1 == 0
+    got = beam_step(h, dw.weight, odd, 1, cur, 10)
+    want = beam_step(h, dw.weight, odd, 1, cur, 10, index=None)
+    assert _compare_steps(got, want) > 0.99
+    assert bool((got[2][got[0] >= 0] >= 8).all())
+    _device_status_ok()
