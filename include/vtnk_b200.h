@@ -178,8 +178,9 @@ int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk
                    void* stream);
 
 /* Beam merge (rectokens/decoding/constrained_decoding.py:305-349, next node
- * :368-383).  level 0: each of the B queries keeps its k best of n_cand
- * candidates (rows = B).  level > 0: total = prev_logp[parent] + cand logp over
+ * :368-383).  Inputs are vtnk_beam_step's outputs: a candidate whose logit is
+ * -inf is missing (its token and node are -1).  level 0: each of the B
+ * queries keeps its k best of n_cand candidates (rows = B).  level > 0: total = prev_logp[parent] + cand logp over
  * the k * n_cand candidates of a query (rows = B * k), the k best kept, ties to
  * the lower candidate index.  prev_ids [B*k, level] int64; out_ids
  * [B*k, level+1]; out_logp, out_node, out_parent [B*k]. */

@@ -229,7 +229,8 @@ merge_kernel(const MergeArgs p) {
   for (int c = lane; c < ncand; c += 32) {
     const int64_t row = p.level == 0 ? b : b * p.k + c / p.n_cand;
     const int64_t t = p.cand_tok[base + c];
-    const float lp = (t >= 0) ? p.cand_logit[base + c] - p.row_lse[row] : -INFINITY;
+    const float lv = p.cand_logit[base + c];  // -inf: a missing candidate
+    const float lp = (lv > -INFINITY) ? lv - p.row_lse[row] : -INFINITY;
     tot[c] = p.level == 0 ? lp : p.prev_logp[row] + lp;
     tok[c] = static_cast<int>(t);
   }
@@ -306,7 +307,7 @@ merge_sorted_kernel(const MergeArgs p) {
     const int dq = 32 / per_q, dc = 32 - dq * per_q;
 #pragma unroll 8
     for (int t = lane; t < total; t += 32) {
-      st[q * stride + c] = (p.cand_tok[e0 + t] >= 0) ? p.cand_logit[e0 + t] : -INFINITY;
+      st[q * stride + c] = p.cand_logit[e0 + t];  // -inf: a missing candidate
       q += dq;
       c += dc;
       if (c >= per_q) {
@@ -345,7 +346,7 @@ merge_sorted_kernel(const MergeArgs p) {
 #pragma unroll
       for (int i = 0; i < KM; ++i) {
         if (i >= L || pos[i] >= n) continue;
-        const float lp = head[i] - ls[i];
+        const float lp = head[i] > -INFINITY ? head[i] - ls[i] : -INFINITY;
         const float v = p.level == 0 ? lp : pv[i] + lp;
         const int c = i * n + pos[i];
         if (v > bv || (v == bv && c < bc)) {
@@ -426,7 +427,7 @@ merge_group_kernel(const MergeArgs p) {
     const int total = static_cast<int>(nq64) * per_q;
     const int64_t e0 = q0 * per_q;
     for (int t = threadIdx.x; t < total; t += 128)
-      gsm[t] = (p.cand_tok[e0 + t] >= 0) ? p.cand_logit[e0 + t] : -INFINITY;
+      gsm[t] = p.cand_logit[e0 + t];  // -inf: a missing candidate
   }
   __syncthreads();
   const int g = threadIdx.x / G;        // query slot in the block
@@ -451,7 +452,8 @@ merge_group_kernel(const MergeArgs p) {
       float v = -INFINITY;
       int c = INT_MAX;
       if (has && pos < n) {
-        const float lp = my[li * n + pos] - ls;
+        const float lv = my[li * n + pos];
+        const float lp = lv > -INFINITY ? lv - ls : -INFINITY;
         v = p.level == 0 ? lp : pv + lp;
         c = li * n + pos;
       }
