@@ -169,7 +169,8 @@ SearchLayout search_layout(const vtnk_search_t* s) {
 int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr, int64_t mb,
             int64_t n_cand, const vtnk_child_index_t* index, int64_t* cand_tok,
             float* cand_logit, int64_t* cand_node, float* row_lse, int sample, uint64_t seed,
-            const float* temperature, float* sample_f, bool stream_k, cudaStream_t s) {
+            const float* temperature, float* sample_f, bool stream_k, cudaStream_t s,
+            const TcArgs* l0 = nullptr) {
   if (tc_enabled() && index && index->masks && lin->dtype == VTNK_BF16 && lin->b_stride_k == 1 &&
       lin->rows >= 128) {
     TcArgs t{};
@@ -199,6 +200,12 @@ int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t*
     t.seed = seed;
     t.temperature = temperature;
     t.sample_f = sample_f;
+    if (l0) {
+      t.l0_ids = l0->l0_ids;
+      t.l0_logp = l0->l0_logp;
+      t.l0_node = l0->l0_node;
+      t.l0_k = l0->l0_k;
+    }
     if (stream_k) {
       const SkWorkspace w = sk_workspace(s);
       t.sk_part = w.part;
@@ -494,17 +501,33 @@ int beam_search_run(const vtnk_search_t* s, void* workspace, size_t workspace_by
     rc = check_linear(&lin);
     if (rc) return rc;
     const vtnk_child_index_t* idx = s->index ? &s->index[level] : nullptr;
-    rc = beam_step_impl(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand, idx,
-                        cand_tok, cand_logit, cand_node, lse, stream_k, st);
-    if (rc) return rc;
     const bool last = level + 1 == s->levels;
     const int slot = static_cast<int>(level & 1);
     int64_t* ids = last ? out_ids : static_cast<int64_t*>(at(L.ids[slot]));
     float* logp = last ? out_logp : static_cast<float*>(at(L.logp[slot]));
     int64_t* node = last ? out_node : static_cast<int64_t*>(at(L.node[slot]));
-    rc = vtnk_beam_merge(level, s->batch, s->beams, s->n_cand, cand_tok, cand_logit, cand_node, lse,
-                         prev_logp, prev_ids, ids, logp, node, parent, stream);
-    if (rc) return rc;
+    // Level 0 has one candidate list per query, so its merge is the list
+    // itself: the tile kernel writes the beams directly when it takes the
+    // level (k <= n_cand); otherwise the step and the merge run as below.
+    rc = VTNK_ERR_UNSUPPORTED;
+    if (level == 0 && s->beams <= s->n_cand && lin.rows > 0) {
+      TcArgs l0{};
+      l0.l0_ids = ids;
+      l0.l0_logp = logp;
+      l0.l0_node = node;
+      l0.l0_k = static_cast<int>(s->beams);
+      rc = tc_step(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand, idx,
+                   nullptr, nullptr, nullptr, nullptr, 0, 0, nullptr, nullptr, stream_k, st, &l0);
+      if (rc != VTNK_OK && rc != VTNK_ERR_UNSUPPORTED) return rc;
+    }
+    if (rc == VTNK_ERR_UNSUPPORTED) {
+      rc = beam_step_impl(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand,
+                          idx, cand_tok, cand_logit, cand_node, lse, stream_k, st);
+      if (rc) return rc;
+      rc = vtnk_beam_merge(level, s->batch, s->beams, s->n_cand, cand_tok, cand_logit,
+                           cand_node, lse, prev_logp, prev_ids, ids, logp, node, parent, stream);
+      if (rc) return rc;
+    }
     prev_node = node;
     prev_logp = logp;
     prev_ids = ids;

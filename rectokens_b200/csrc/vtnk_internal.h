@@ -74,6 +74,13 @@ struct TcArgs {
   uint64_t seed;
   const float* temperature;  // device scalar or nullptr (1)
   float* sample_f;           // optional: sampled token id as float, -1 when none
+  // Level 0 of a beam search (every row its own query): the k <= n_cand best
+  // candidates of each row become its beams directly -- ids [rows*k],
+  // logp = logit - lse, node -- in place of the beam merge (optional).
+  int64_t* l0_ids;
+  float* l0_logp;
+  int64_t* l0_node;
+  int l0_k;
   // Stream-K workspace (all nullptr: whole tiles round-robin only).
   float* sk_part;                // sk_cap_pairs * 512 KB
   unsigned long long* sk_count;  // sk_count_cap words, zero before first use

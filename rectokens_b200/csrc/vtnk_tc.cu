@@ -138,6 +138,10 @@ struct Params {
   uint64_t seed;             // sampling: Philox key
   const float* temperature;  // sampling: device scalar (nullptr: 1)
   float* sample_f;           // sampling: token id as float, -1 when none (optional)
+  int64_t* l0_ids;           // level 0 of a beam search: beams written directly (optional)
+  float* l0_logp;
+  int64_t* l0_node;
+  int l0_k;
   // Schedule: tiles [0, dp_tiles) go to pairs round-robin (whole tiles); the
   // k-block iterations of tiles [dp_tiles, n_tiles) are split evenly over the
   // first sk_pairs pairs (stream-K).  A tile split between pairs is summed
@@ -1278,6 +1282,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           if (p.cand_tok) p.cand_tok[o + j] = tok;
           if (p.cand_logit) p.cand_logit[o + j] = lv;  // sampling: the winning score
           if (p.cand_node) p.cand_node[o + j] = node;
+          if (p.l0_ids && j < p.l0_k) {  // level 0: the row's j-th best child is its beam j
+            const int64_t ob = row * p.l0_k + j;
+            p.l0_ids[ob] = tok;
+            p.l0_logp[ob] = lv > -INFINITY ? lv - lse : -INFINITY;
+            p.l0_node[ob] = node;
+          }
           if (SAMPLE && p.sample_f) p.sample_f[row] = tok >= 0 ? static_cast<float>(tok) : -1.f;
         }
         if (p.row_lse) p.row_lse[row] = lse;
@@ -1472,6 +1482,10 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.seed = t.seed;
   p.temperature = t.temperature;
   p.sample_f = t.sample_f;
+  p.l0_ids = t.l0_ids;
+  p.l0_logp = t.l0_logp;
+  p.l0_node = t.l0_node;
+  p.l0_k = t.l0_k;
   // Schedule.  Whole tiles round-robin over the pairs; when the last round
   // would leave pairs idle, the last two rounds' tiles are split into equal
   // k-block ranges instead (at least MIN_SEG k-blocks per pair).
