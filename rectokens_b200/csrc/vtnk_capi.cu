@@ -170,7 +170,7 @@ int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t*
             int64_t n_cand, const vtnk_child_index_t* index, int64_t* cand_tok,
             float* cand_logit, int64_t* cand_node, float* row_lse, int sample, uint64_t seed,
             const float* temperature, float* sample_f, bool stream_k, cudaStream_t s,
-            const TcArgs* l0 = nullptr) {
+            const TcArgs* l0 = nullptr, bool pdl = false) {
   if (tc_enabled() && index && index->masks && lin->dtype == VTNK_BF16 && lin->b_stride_k == 1 &&
       lin->rows >= 128) {
     TcArgs t{};
@@ -200,6 +200,7 @@ int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t*
     t.seed = seed;
     t.temperature = temperature;
     t.sample_f = sample_f;
+    t.pdl = pdl;
     if (l0) {
       t.l0_ids = l0->l0_ids;
       t.l0_logp = l0->l0_logp;
@@ -223,10 +224,10 @@ int tc_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t*
 int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk_csr_t* csr,
                    int64_t mb, int64_t n_cand, const vtnk_child_index_t* index,
                    int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
-                   bool stream_k, cudaStream_t s) {
+                   bool stream_k, cudaStream_t s, bool pdl = false) {
   if (lin->rows == 0) return VTNK_OK;
   const int rc = tc_step(lin, cur_node, csr, mb, n_cand, index, cand_tok, cand_logit, cand_node,
-                         row_lse, 0, 0, nullptr, nullptr, stream_k, s);
+                         row_lse, 0, 0, nullptr, nullptr, stream_k, s, nullptr, pdl);
   if (rc != VTNK_ERR_UNSUPPORTED) return rc;
   RowsArgs p = rows_from(lin, cur_node, csr, mb);
   p.k = static_cast<int>(n_cand);
@@ -239,6 +240,45 @@ int beam_step_impl(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk
 }
 
 }  // namespace
+
+int merge_impl(int64_t level, int64_t B, int64_t k, int64_t n_cand, const int64_t* cand_tok,
+               const float* cand_logit, const int64_t* cand_node, const float* row_lse,
+               const float* prev_logp, const int64_t* prev_ids, int64_t* out_ids, float* out_logp,
+               int64_t* out_node, int64_t* out_parent, bool pdl, cudaStream_t stream) {
+  VTNK_REQUIRE(level >= 0 && B >= 0 && k >= 1 && n_cand >= 1, "bad merge sizes");
+  VTNK_REQUIRE(level > 0 || k <= n_cand, "first level needs k <= n_cand");
+  VTNK_REQUIRE(B == 0 || (cand_tok && cand_logit && cand_node && row_lse && out_ids && out_logp &&
+                          out_node && out_parent),
+               "NULL pointer");
+  VTNK_REQUIRE(level == 0 || B == 0 || (prev_logp && prev_ids), "NULL previous beams");
+  MergeArgs p{};
+  p.level = level;
+  p.B = B;
+  p.k = static_cast<int>(k);
+  p.n_cand = static_cast<int>(n_cand);
+  p.cap = static_cast<int>(level == 0 ? n_cand : k * n_cand);
+  p.cand_tok = cand_tok;
+  p.cand_logit = cand_logit;
+  p.cand_node = cand_node;
+  p.row_lse = row_lse;
+  p.prev_logp = prev_logp;
+  p.prev_ids = prev_ids;
+  p.out_ids = out_ids;
+  p.out_logp = out_logp;
+  p.out_node = out_node;
+  p.out_parent = out_parent;
+  p.pdl = pdl;
+  return launch_merge(p, stream);
+}
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("VTNK_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 }  // namespace vtnk
 
 using namespace vtnk;
@@ -421,29 +461,8 @@ int vtnk_beam_merge(int64_t level, int64_t B, int64_t k, int64_t n_cand,
                     const float* row_lse, const float* prev_logp, const int64_t* prev_ids,
                     int64_t* out_ids, float* out_logp, int64_t* out_node, int64_t* out_parent,
                     void* stream) {
-  VTNK_REQUIRE(level >= 0 && B >= 0 && k >= 1 && n_cand >= 1, "bad merge sizes");
-  VTNK_REQUIRE(level > 0 || k <= n_cand, "first level needs k <= n_cand");
-  VTNK_REQUIRE(B == 0 || (cand_tok && cand_logit && cand_node && row_lse && out_ids && out_logp &&
-                          out_node && out_parent),
-               "NULL pointer");
-  VTNK_REQUIRE(level == 0 || B == 0 || (prev_logp && prev_ids), "NULL previous beams");
-  MergeArgs p{};
-  p.level = level;
-  p.B = B;
-  p.k = static_cast<int>(k);
-  p.n_cand = static_cast<int>(n_cand);
-  p.cap = static_cast<int>(level == 0 ? n_cand : k * n_cand);
-  p.cand_tok = cand_tok;
-  p.cand_logit = cand_logit;
-  p.cand_node = cand_node;
-  p.row_lse = row_lse;
-  p.prev_logp = prev_logp;
-  p.prev_ids = prev_ids;
-  p.out_ids = out_ids;
-  p.out_logp = out_logp;
-  p.out_node = out_node;
-  p.out_parent = out_parent;
-  return launch_merge(p, as_stream(stream));
+  return merge_impl(level, B, k, n_cand, cand_tok, cand_logit, cand_node, row_lse, prev_logp,
+                    prev_ids, out_ids, out_logp, out_node, out_parent, false, as_stream(stream));
 }
 
 size_t vtnk_beam_search_workspace_bytes(const vtnk_search_t* s) {
@@ -521,11 +540,16 @@ int beam_search_run(const vtnk_search_t* s, void* workspace, size_t workspace_by
       if (rc != VTNK_OK && rc != VTNK_ERR_UNSUPPORTED) return rc;
     }
     if (rc == VTNK_ERR_UNSUPPORTED) {
+      // After the first kernel of the search, step and merge are chained
+      // with programmatic dependent launch: each waits for its predecessor's
+      // results inside the kernel, so launch gaps and the next level's
+      // operand stream overlap the previous kernel's tail.
+      const bool pdl = level > 0 && pdl_enabled();
       rc = beam_step_impl(&lin, prev_node, &s->csr, s->layer_max_branches[level], s->n_cand,
-                          idx, cand_tok, cand_logit, cand_node, lse, stream_k, st);
+                          idx, cand_tok, cand_logit, cand_node, lse, stream_k, st, pdl);
       if (rc) return rc;
-      rc = vtnk_beam_merge(level, s->batch, s->beams, s->n_cand, cand_tok, cand_logit,
-                           cand_node, lse, prev_logp, prev_ids, ids, logp, node, parent, stream);
+      rc = merge_impl(level, s->batch, s->beams, s->n_cand, cand_tok, cand_logit, cand_node, lse,
+                      prev_logp, prev_ids, ids, logp, node, parent, pdl, st);
       if (rc) return rc;
     }
     prev_node = node;

@@ -47,7 +47,19 @@ struct MergeArgs {
   float* out_logp;
   int64_t* out_node;
   int64_t* out_parent;
+  // Programmatic dependent launch inside a search: the merge may be scheduled
+  // before the step kernel ends (it waits for the step's results itself).
+  bool pdl;
 };
+
+// Whether searches chain their launches with programmatic dependent launch
+// (VTNK_PDL=0 turns it off).
+bool pdl_enabled();
+// vtnk_beam_merge with the launch mode (pdl: inside a search, see MergeArgs).
+int merge_impl(int64_t level, int64_t B, int64_t k, int64_t n_cand, const int64_t* cand_tok,
+               const float* cand_logit, const int64_t* cand_node, const float* row_lse,
+               const float* prev_logp, const int64_t* prev_ids, int64_t* out_ids, float* out_logp,
+               int64_t* out_node, int64_t* out_parent, bool pdl, cudaStream_t stream);
 
 // Tensor-core beam step (vtnk_tc.cu).
 struct TcArgs {
@@ -81,6 +93,7 @@ struct TcArgs {
   float* l0_logp;
   int64_t* l0_node;
   int l0_k;
+  bool pdl;  // launch as a programmatic dependent of the previous kernel (inside a search)
   // Stream-K workspace (all nullptr: whole tiles round-robin only).
   float* sk_part;                // sk_cap_pairs * 512 KB
   unsigned long long* sk_count;  // sk_count_cap words, zero before first use

@@ -414,14 +414,10 @@ merge_sorted_kernel(const MergeArgs p) {
 // memory by coalesced loads of the block's queries.  A query with an
 // unsorted list is merged by its lane 0 with the exact successor scan.
 template <int G>
-__global__ void __launch_bounds__(128)
-merge_group_kernel(const MergeArgs p) {
-  extern __shared__ float gsm[];
-  constexpr int QPB = 128 / G;  // queries per block
-  const int n = p.n_cand;
-  const int L = p.level == 0 ? 1 : p.k;
-  const int per_q = L * n;
-  const int64_t q0 = static_cast<int64_t>(blockIdx.x) * QPB;
+__device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm, int64_t q0,
+                                                  int n, int L, int per_q) {
+  constexpr int QPB = 128 / G;
+  __syncthreads();  // the previous block's readers are done with gsm
   {
     const int64_t nq64 = p.B - q0 < QPB ? p.B - q0 : QPB;
     const int total = static_cast<int>(nq64) * per_q;
@@ -433,7 +429,7 @@ merge_group_kernel(const MergeArgs p) {
   const int g = threadIdx.x / G;        // query slot in the block
   const int li = threadIdx.x % G;       // list (parent) index
   const int64_t b = q0 + g;
-  if (b >= p.B) return;                 // whole groups retire together
+  if (b >= p.B) return;                 // whole groups retire together (the last block)
   const unsigned gmask = (G == 32) ? 0xffffffffu : (0xffffu << ((threadIdx.x & 31) & 16));
   const float* my = gsm + g * per_q;
   const int64_t row0 = p.level == 0 ? b : b * p.k;
@@ -517,6 +513,26 @@ merge_group_kernel(const MergeArgs p) {
   p.out_ids[o * (p.level + 1) + p.level] = p.cand_tok[e];
   for (int t = 0; t < p.level; ++t)
     p.out_ids[o * (p.level + 1) + t] = p.prev_ids[parent * p.level + t];
+}
+
+template <int G>
+__global__ void __launch_bounds__(128)
+merge_group_kernel(const MergeArgs p) {
+  extern __shared__ float gsm[];
+  // Launched as a programmatic dependent of the step kernel (inside a
+  // search): wait for its results, then let the next level's step kernel be
+  // scheduled as this merge drains.  Both are no-ops in a plain launch.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  constexpr int QPB = 128 / G;  // queries per block
+  const int n = p.n_cand;
+  const int L = p.level == 0 ? 1 : p.k;
+  const int per_q = L * n;
+  // grid-stride over blocks of QPB queries
+  for (int64_t q0 = static_cast<int64_t>(blockIdx.x) * QPB; q0 < p.B;
+       q0 += static_cast<int64_t>(gridDim.x) * QPB) {
+    merge_group_block<G>(p, gsm, q0, n, L, per_q);
+  }
 }
 
 template <typename T>
@@ -642,19 +658,21 @@ int launch_merge(const MergeArgs& p, cudaStream_t s) {
     const int G = p.k <= 16 ? 16 : 32;
     const size_t sm = static_cast<size_t>(128 / G) * lists * p.n_cand * sizeof(float);
     if (sm <= 96 * 1024) {
-      const int grid = static_cast<int>((p.B + 128 / G - 1) / (128 / G));
-      if (G == 16) {
-        if (sm > 48 * 1024)
-          cudaFuncSetAttribute(merge_group_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(sm));
-        merge_group_kernel<16><<<grid, 128, sm, s>>>(p);
-      } else {
-        if (sm > 48 * 1024)
-          cudaFuncSetAttribute(merge_group_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               static_cast<int>(sm));
-        merge_group_kernel<32><<<grid, 128, sm, s>>>(p);
-      }
-      return cuda_status(cudaGetLastError(), "merge_group_kernel launch");
+      const int64_t grid = (p.B + 128 / G - 1) / (128 / G);
+      auto k = G == 16 ? merge_group_kernel<16> : merge_group_kernel<32>;
+      if (sm > 48 * 1024)
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(static_cast<unsigned>(grid));
+      cfg.blockDim = dim3(128);
+      cfg.dynamicSmemBytes = sm;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = p.pdl ? 1 : 0;
+      return cuda_status(cudaLaunchKernelEx(&cfg, k, p), "merge_group_kernel launch");
     }
   }
   const size_t per_warp = 32 * static_cast<size_t>(lists * p.n_cand + 1) * sizeof(float);

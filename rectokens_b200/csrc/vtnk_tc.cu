@@ -790,6 +790,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_after();
   const uint32_t tmem = S.tmem_base;
   if (threadIdx.x == 0) TRACE(1);
+  // Programmatic dependent launch (inside a search): the next kernel (the
+  // merge) may be scheduled now; it waits for this grid's results itself.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   if (warp == 0) {
     // ---------------------------------------------------------------- TMA producer (both CTAs)
@@ -913,6 +916,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
   } else {
     // ---------------------------------------------------------------- epilogue
+    // The rows' nodes (and the candidate buffers) belong to the previous
+    // kernel of a search: wait for it to finish.  The producer and the MMA
+    // issuer only read the hidden states and the head, which no kernel of
+    // the search writes, so they start streaming at once.  A no-op in a
+    // plain launch.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int lg = warp & 3;             // TMEM lane group this warp may access
     // pair: half 0 = columns 0..127 (+ merge, outputs), half 1 = 128..255;
     // split: the same two halves of this CTA's 128 columns
@@ -1412,7 +1421,7 @@ int sm_count() {
 
 template <int NC, bool SAMPLE, bool SPLIT>
 int launch_variant(const CUtensorMap& a, const CUtensorMap& w, const Params& p, int pairs,
-                   cudaStream_t s) {
+                   bool pdl, cudaStream_t s) {
   auto k = beam_step_kernel<NC, SAMPLE, SPLIT>;
   constexpr size_t smem = smem_bytes<SPLIT>();
   // The shared-memory opt-in is per kernel and device; set it once each.
@@ -1425,15 +1434,24 @@ int launch_variant(const CUtensorMap& a, const CUtensorMap& w, const Params& p, 
     if (e != cudaSuccess) return cuda_status(e, "beam_step_tc smem attribute");
     if (dev < 64) set_on.fetch_or(1ull << dev, std::memory_order_relaxed);
   }
-  k<<<2 * pairs, THREADS, smem, s>>>(a, w, p);
-  return cuda_status(cudaGetLastError(), "beam_step_tc launch");
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+  cfg.blockDim = dim3(THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cuda_status(cudaLaunchKernelEx(&cfg, k, a, w, p), "beam_step_tc launch");
 }
 
 template <int NC, bool SAMPLE = false>
 int launch_nc(const CUtensorMap& a, const CUtensorMap& w, const Params& p, int pairs, bool split,
-              cudaStream_t s) {
-  return split ? launch_variant<NC, SAMPLE, true>(a, w, p, pairs, s)
-               : launch_variant<NC, SAMPLE, false>(a, w, p, pairs, s);
+              bool pdl, cudaStream_t s) {
+  return split ? launch_variant<NC, SAMPLE, true>(a, w, p, pairs, pdl, s)
+               : launch_variant<NC, SAMPLE, false>(a, w, p, pairs, pdl, s);
 }
 
 }  // namespace tc
@@ -1537,18 +1555,18 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
     set_error("cuTensorMapEncodeTiled failed");
     return VTNK_ERR_CUDA;
   }
-  if (t.sample) return t.n_cand == 1 ? launch_nc<1, true>(ma, mw, p, np, split, s) : VTNK_ERR_UNSUPPORTED;
+  if (t.sample) return t.n_cand == 1 ? launch_nc<1, true>(ma, mw, p, np, split, t.pdl, s) : VTNK_ERR_UNSUPPORTED;
   switch (t.n_cand) {  // exact widths for the common beam sizes
-    case 1: return launch_nc<1>(ma, mw, p, np, split, s);
-    case 5: return launch_nc<5>(ma, mw, p, np, split, s);
-    case 10: return launch_nc<10>(ma, mw, p, np, split, s);
-    case 20: return launch_nc<20>(ma, mw, p, np, split, s);
+    case 1: return launch_nc<1>(ma, mw, p, np, split, t.pdl, s);
+    case 5: return launch_nc<5>(ma, mw, p, np, split, t.pdl, s);
+    case 10: return launch_nc<10>(ma, mw, p, np, split, t.pdl, s);
+    case 20: return launch_nc<20>(ma, mw, p, np, split, t.pdl, s);
     default: break;
   }
-  if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, np, split, s);
-  if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, np, split, s);
-  if (t.n_cand <= 16) return launch_nc<16>(ma, mw, p, np, split, s);
-  return launch_nc<32>(ma, mw, p, np, split, s);
+  if (t.n_cand <= 4) return launch_nc<4>(ma, mw, p, np, split, t.pdl, s);
+  if (t.n_cand <= 8) return launch_nc<8>(ma, mw, p, np, split, t.pdl, s);
+  if (t.n_cand <= 16) return launch_nc<16>(ma, mw, p, np, split, t.pdl, s);
+  return launch_nc<32>(ma, mw, p, np, split, t.pdl, s);
 }
 
 int launch_build_child_index(const Csr& csr, uint32_t* masks, uint32_t* flags, int64_t node_lo,
