@@ -413,6 +413,13 @@ merge_sorted_kernel(const MergeArgs p) {
 // round r's choice and writes output beam r.  Candidates are staged in shared
 // memory by coalesced loads of the block's queries.  A query with an
 // unsorted list is merged by its lane 0 with the exact successor scan.
+// Order-preserving 32-bit key of a float (a > b  <=>  key(a) > key(b); -0
+// and +0 share a key).  No NaN reaches the merge.
+__device__ __forceinline__ unsigned order_key(float f) {
+  const unsigned u = __float_as_uint(f + 0.0f);  // -0 -> +0
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 template <int G>
 __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm, int64_t q0,
                                                   int n, int L, int per_q) {
@@ -453,16 +460,17 @@ __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm
         v = p.level == 0 ? lp : pv + lp;
         c = li * n + pos;
       }
-#pragma unroll
-      for (int o = G / 2; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(gmask, v, o);
-        const int oc = __shfl_xor_sync(gmask, c, o);
-        if (ov > v || (ov == v && oc < c)) {
-          v = ov;
-          c = oc;
-        }
-      }
-      if (has && c == li * n + pos) ++pos;  // the winning list advances
+      // best value over the group: one max-reduction of an order-preserving
+      // key, then the lowest lane holding it (lower parent, and within a
+      // list the head is its lowest remaining slot: the reference's tie order)
+      const unsigned key = order_key(v);
+      const unsigned best = __reduce_max_sync(gmask, key);
+      const unsigned holders = __ballot_sync(gmask, key == best && c != INT_MAX) & gmask;
+      const int wl = __ffs(holders) - 1;
+      const bool mine = (threadIdx.x & 31) == wl;
+      v = __shfl_sync(gmask, v, wl);
+      c = __shfl_sync(gmask, c, wl);
+      if (mine) ++pos;  // the winning list advances
       if (li == r) {
         my_c = c;
         my_v = v;
