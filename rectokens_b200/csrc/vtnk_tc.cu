@@ -8,17 +8,24 @@
 // that are not children of a row's node are dropped in the epilogue, using
 // the depth's child-bitmask index (32 bytes per node, built once per trie).
 //
-// CTA layout (persistent, one CTA per SM, 320 threads):
-//   warp 0      TMA producer      A tile [128 x 64] + W tile [256 x 64] per stage
-//   warp 1      MMA issuer        tcgen05.mma.cta_group::1.kind::f16, M=128 N=256 K=16
-//                                 (also allocates / frees 512 TMEM columns)
-//   warps 2..9  epilogue          thread = row: tcgen05.ld 32x32b, mask, top-n, LSE;
-//                                 two warps per TMEM lane group split the 256
-//                                 columns, the upper half hands its partial
-//                                 result to the lower half
-// Shared memory: 3 stages x 48 KB operand ring (SWIZZLE_128B, K-major), the
-// epilogue's chunk staging and hand-off buffers, the window's bias, mbarriers.  TMEM holds two 128 x 256 fp32 accumulators so
-// the epilogue of tile i overlaps the MMAs of tile i + 1.
+// CTA layout (persistent; a cluster of two CTAs on two SMs; 320 threads each):
+//   warp 0      TMA producer      per stage: this CTA's A tile [128 x 64] and half
+//                                 of the W window [128 x 64] (SWIZZLE_128B, K-major)
+//   warp 1      MMA issuer        pair variant: the leader issues
+//                                 tcgen05.mma.cta_group::2.kind::f16, M=256 N=256 K=16
+//                                 over both CTAs' operands; split variant: each CTA
+//                                 issues cta_group::1 M=128 N=128 on its own half of
+//                                 the window.  Also allocates / frees TMEM (two
+//                                 accumulators, so the epilogue of tile i overlaps
+//                                 the MMAs of tile i + 1)
+//   warps 2..9  epilogue          thread = row: tcgen05.ld 32x32b, mask, log-sum-exp
+//                                 and top-n (or Gumbel-max); two warps per TMEM lane
+//                                 group split the columns, the upper half hands its
+//                                 partial result to the lower half (split variant:
+//                                 then CTA 1 to CTA 0 through distributed shared
+//                                 memory)
+// Shared memory: a 5-stage x 32 KB operand ring (4 in the split variant), the
+// epilogue's chunk staging and hand-off buffers, the window's bias, mbarriers.
 //
 // Every mbarrier wait is bounded in time; on expiry the CTA records a status
 // code in a device word (read by vtnk_device_status), drains its in-flight
