@@ -517,9 +517,9 @@ def main():
                 "unit": "TFLOP/s"}
     roof["frac"] = roof["achieved"] / roof["peak"]
     # DRAM bytes per hidden-state row of the step kernel, from the committed ncu
-    # capture (profiles/tc_beam_step_cfg5.md: 610.7 MB for 81,920 rows at level
+    # capture (profiles/tc_beam_step_cfg5.md: 611.1 MB for 81,920 rows at level
     # 1), scaled to this search's rows; null for other workloads
-    roof["traffic"] = (round(7455.0 * sum(rows_l)) if args.workload == "cfg5" else None)
+    roof["traffic"] = (round(7460.0 * sum(rows_l)) if args.workload == "cfg5" else None)
     roof["traffic_note"] = "scaled from a level-1 ncu capture (profiles/tc_beam_step_cfg5.md)"
     roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json burst figures)"
     roof["kernel"] = "vtnk beam-step kernel, all levels of one search"
