@@ -89,6 +89,14 @@ constexpr int MAX_NC = 32;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
 
+// The split variant's cross-CTA hand-off buffers (none in the pair variant).
+template <bool SPLIT>
+struct XMerge {
+  float x[4][MAX_NC + MAX_NC / 4 + 2][32];
+};
+template <>
+struct XMerge<false> {};
+
 // SPLIT: the split-window variant (see beam_step_kernel) with one stage
 // fewer and the buffers of its cross-CTA hand-off.
 template <bool SPLIT>
@@ -98,7 +106,7 @@ struct SharedT {
   float chunk_x[EPI_WARPS][32][32];    // epilogue: one 32-column chunk per warp, [col][lane]
   float merge[4][MAX_NC + MAX_NC / 4 + 2][32];  // upper-half -> lower-half partial results:
                                                 // NC values, NC byte-packed columns, max, sum
-  float xmerge[SPLIT ? 4 : 1][MAX_NC + MAX_NC / 4 + 2][32];  // split: window half 1 -> half 0
+  XMerge<SPLIT> xm;  // split: window half 1 -> half 0 (empty in the pair variant)
   float bias[BN];
   uint64_t full[ST];
   uint64_t empty[ST];
@@ -1235,14 +1243,14 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // at cluster scope on the barriers); CTA 0 writes the outputs.
         if (rank == 1) {
           if (!warp_wait_phase_cluster(&S.xmerge_empty[lg], (xit & 1) ^ 1, abort, 8)) break;
-          put_list([&](int r, float v) { st_cluster_f32(map_to_rank(&S.xmerge[lg][r][lane], 0), v); });
+          put_list([&](int r, float v) { st_cluster_f32(map_to_rank(&S.xm.x[lg][r][lane], 0), v); });
           warp_arrive_cluster(map_to_rank(&S.xmerge_full[lg], 0));
           ++xit;
           PROF_ACC(pe_tmem, t_tm);
           continue;
         }
         if (!warp_wait_phase_cluster(&S.xmerge_full[lg], xit & 1, abort, 9)) break;
-        absorb(S.xmerge[lg]);
+        absorb(S.xm.x[lg]);
         warp_arrive_cluster(map_to_rank(&S.xmerge_empty[lg], 1));
         ++xit;
       }
