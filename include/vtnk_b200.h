@@ -254,6 +254,19 @@ int vtnk_synth_normal(uint64_t seed, uint64_t stream_id, int64_t row0, int64_t r
  * bounded waits). */
 int vtnk_device_status(int reset);
 
+/* Bound, in nanoseconds, of every wait inside the tile kernel (process-wide,
+ * read at each launch; 0 restores the default of 2 s).  A wait that runs out
+ * makes its CTA drain its copies and MMAs with bounded waits, free its tensor
+ * memory and exit; vtnk_device_status then reports VTNK_ERR_DEVICE.  No
+ * reference counterpart (the reference's kernels do not wait on barriers). */
+int vtnk_set_wait_limit_ns(uint64_t ns);
+
+/* Test hook for the failure path above: the next n tile-kernel launches
+ * issue no operand copies, so their first wait runs out after the wait
+ * limit and the launch ends with the device status set (its outputs are
+ * then undefined).  n = 0 cancels.  No reference counterpart. */
+int vtnk_debug_stall_launches(int n);
+
 /* Human-readable description of the last error on this host thread. */
 const char* vtnk_last_error(void);
 

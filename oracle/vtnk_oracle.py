@@ -89,6 +89,20 @@ def branch_logits(a, b, bias, valid_idxs, acc=np.float64):
     bt = np.asarray(b).T  # (N, H), weight rows
     B, mb = valid_idxs.shape
     out = np.full((B, mb), -np.inf, dtype=np.float64)
+    N, H = bt.shape
+    if N * H <= (1 << 24) and B * mb >= 4 * N:
+        # many rows over a small head: one GEMM against every head row, then
+        # the valid columns (the same dot products, summed by BLAS)
+        wt = bt.astype(acc, copy=False)
+        rchunk = max(1, (1 << 24) // N)
+        for r0 in range(0, B, rchunk):
+            vi = valid_idxs[r0:r0 + rchunk]
+            full = a[r0:r0 + rchunk].astype(acc, copy=False) @ wt.T        # (r, N)
+            vals = np.take_along_axis(full, np.maximum(vi, 0), axis=1)
+            if bias is not None:
+                vals = vals + np.asarray(bias, dtype=acc)[np.maximum(vi, 0)]
+            out[r0:r0 + rchunk] = np.where(vi >= 0, vals, -np.inf)
+        return out.astype(np.float32)
     chunk = max(1, (1 << 25) // max(1, mb * a.shape[1]))  # bound the gathered block
     for r0 in range(0, B, chunk):
         vi = valid_idxs[r0:r0 + chunk]

@@ -3,13 +3,11 @@
 Drop-in for the constrained-decoding hot path of RecTokens
 (``rectokens.ops.constrained_node_transition`` and the beam search of
 ``rectokens.decoding.constrained_decoding``), backed by the CUDA kernels of
-``libvtnk_b200.so``.  There is no CPU fallback: on a machine with a GPU the
-library is loaded at import and a missing build raises.
+``libvtnk_b200.so``.  There is no CPU fallback: the library is loaded on the
+first call of an op (a missing build raises there), so importing the package
+alone maps no native code.
 """
 
-import torch
-
-from rectokens_b200 import _lib
 from rectokens_b200.decoding.beam_search import (
     BeamSearchResult,
     constrained_beam_search,
@@ -29,9 +27,6 @@ from rectokens_b200.schemas import (
     GenerationConfig,
     GenerationState,
 )
-
-if torch.cuda.is_available():
-    _lib.lib()
 
 __all__ = [
     "BeamSearchResult",

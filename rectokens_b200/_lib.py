@@ -33,6 +33,8 @@ EXPORTS = (
     "vtnk_beam_search_noalloc",
     "vtnk_synth_normal",
     "vtnk_device_status",
+    "vtnk_set_wait_limit_ns",
+    "vtnk_debug_stall_launches",
     "vtnk_last_error",
     "vtnk_version",
 )
@@ -104,6 +106,10 @@ def lib() -> ctypes.CDLL:
             fn.restype = c_int
         L.vtnk_beam_search_workspace_bytes.argtypes = [POINTER(Search)]
         L.vtnk_beam_search_workspace_bytes.restype = c_size_t
+        L.vtnk_set_wait_limit_ns.argtypes = [c_uint64]
+        L.vtnk_set_wait_limit_ns.restype = c_int
+        L.vtnk_debug_stall_launches.argtypes = [c_int]
+        L.vtnk_debug_stall_launches.restype = c_int
         L.vtnk_device_status.argtypes = [c_int]
         L.vtnk_device_status.restype = c_int
         L.vtnk_last_error.argtypes = []

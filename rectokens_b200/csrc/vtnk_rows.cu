@@ -231,7 +231,8 @@ merge_kernel(const MergeArgs p) {
     const int64_t t = p.cand_tok[base + c];
     const float lv = p.cand_logit[base + c];  // -inf: a missing candidate
     const float lp = (lv > -INFINITY) ? lv - p.row_lse[row] : -INFINITY;
-    tot[c] = p.level == 0 ? lp : p.prev_logp[row] + lp;
+    const float v = p.level == 0 ? lp : p.prev_logp[row] + lp;
+    tot[c] = (v == v) ? v : -INFINITY;  // a NaN score (never produced by the step kernels) ranks last
     tok[c] = static_cast<int>(t);
   }
   __syncwarp();
@@ -347,7 +348,8 @@ merge_sorted_kernel(const MergeArgs p) {
       for (int i = 0; i < KM; ++i) {
         if (i >= L || pos[i] >= n) continue;
         const float lp = head[i] > -INFINITY ? head[i] - ls[i] : -INFINITY;
-        const float v = p.level == 0 ? lp : pv[i] + lp;
+        float v = p.level == 0 ? lp : pv[i] + lp;
+        if (!(v == v)) v = -INFINITY;
         const int c = i * n + pos[i];
         if (v > bv || (v == bv && c < bc)) {
           bv = v;
@@ -377,7 +379,8 @@ merge_sorted_kernel(const MergeArgs p) {
         const int i = c / n;
         const float lv = my[c];
         const float lp = lv > -INFINITY ? lv - p.row_lse[row0 + i] : -INFINITY;
-        const float v = p.level == 0 ? lp : p.prev_logp[row0 + i] + lp;
+        float v = p.level == 0 ? lp : p.prev_logp[row0 + i] + lp;
+        if (!(v == v)) v = -INFINITY;  // NaN ranks last: every round finds a candidate
         const bool after = v < prev_v || (v == prev_v && c > prev_c);
         if (after && (v > bv || (v == bv && c < bc) || bc == INT_MAX)) {
           bv = v;
@@ -487,7 +490,8 @@ __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm
         const int i = c / n;
         const float lv = my[c];
         const float lp = lv > -INFINITY ? lv - p.row_lse[row0 + i] : -INFINITY;
-        const float v = p.level == 0 ? lp : p.prev_logp[row0 + i] + lp;
+        float v = p.level == 0 ? lp : p.prev_logp[row0 + i] + lp;
+        if (!(v == v)) v = -INFINITY;  // NaN ranks last: every round finds a candidate
         const bool after = v < prev_v || (v == prev_v && c > prev_c);
         if (after && (v > bv || (v == bv && c < bc) || bc == INT_MAX)) {
           bv = v;

@@ -87,7 +87,7 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int EPI_WARPS = 8;  // two per TMEM lane group, splitting the 256 columns
 constexpr int MAX_NC = 32;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
-constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // 2 s
+constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // default bound of every wait: 2 s
 
 // The split variant's cross-CTA hand-off buffers (none in the pair variant).
 template <bool SPLIT>
@@ -167,11 +167,18 @@ struct Params {
   float* sk_part;                    // [sk_pairs][2 slots][2 ranks][BM][BN] fp32
   unsigned long long* sk_count;      // [stream-K tiles][2 ranks]: epoch << 32 | k-blocks done
   uint32_t sk_epoch;                 // distinct per launch on the same workspace
+  uint64_t wait_ns;  // bound of every mbarrier wait (ns); on expiry the CTA aborts
+  int stall;         // test hook: the producers issue no copies, so the first wait expires
 };
 
 // ------------------------------------------------------------------ PTX wrappers
 __device__ __forceinline__ uint32_t su32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ int64_t ld_relaxed_s64(const int64_t* q) {
+  int64_t v;
+  asm volatile("ld.relaxed.gpu.global.s64 %0, [%1];" : "=l"(v) : "l"(q) : "memory");
+  return v;
 }
 __device__ __forceinline__ uint64_t gtimer() {
   uint64_t t;
@@ -202,7 +209,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
 // Wait for phase `parity` of barrier b; false when the CTA is aborting or the
 // time limit ran out (then the abort flag and the device status are set).
 __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatile int* abort,
-                                           int code) {
+                                           int code, uint64_t lim) {
   if (mbar_try_wait(b, parity)) return true;
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
@@ -212,7 +219,7 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatil
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
       if (*abort) return false;
-      if (gtimer() - t0 > WAIT_LIMIT_NS || i > (1u << 30)) {
+      if (gtimer() - t0 > lim || i > (1u << 30)) {
         *abort = 1;
         atomicCAS(&g_tc_status, 0, code);
         return false;
@@ -253,7 +260,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* b, uint32_t pari
 }
 // Bounded wait with cluster-scope acquire (for arrivals from the peer CTA).
 __device__ __forceinline__ bool wait_phase_cluster(uint64_t* b, uint32_t parity,
-                                                   volatile int* abort, int code) {
+                                                   volatile int* abort, int code, uint64_t lim) {
   if (mbar_try_wait_cluster(b, parity)) return true;
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
@@ -263,7 +270,7 @@ __device__ __forceinline__ bool wait_phase_cluster(uint64_t* b, uint32_t parity,
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
       if (*abort) return false;
-      if (gtimer() - t0 > WAIT_LIMIT_NS || i > (1u << 30)) {
+      if (gtimer() - t0 > lim || i > (1u << 30)) {
         *abort = 1;
         atomicCAS(&g_tc_status, 0, code);
         return false;
@@ -285,7 +292,7 @@ __device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* m
 // between polls, so 128 waiting threads do not compete with the tensor
 // core's operand reads for shared memory.  Result in every lane.
 __device__ __forceinline__ bool warp_wait_phase(uint64_t* b, uint32_t parity, volatile int* abort,
-                                                int code) {
+                                                int code, uint64_t lim) {
   int ok = 1;
   if ((threadIdx.x & 31) == 0) {
     if (!mbar_try_wait(b, parity)) {
@@ -299,7 +306,7 @@ __device__ __forceinline__ bool warp_wait_phase(uint64_t* b, uint32_t parity, vo
           ok = 0;
           break;
         }
-        if (gtimer() - t0 > WAIT_LIMIT_NS) {
+        if (gtimer() - t0 > lim) {
           *abort = 1;
           atomicCAS(&g_tc_status, 0, code);
           ok = 0;
@@ -331,7 +338,8 @@ __device__ __forceinline__ void warp_arrive_cluster(uint32_t cluster_addr) {
 // warp_wait_phase for a barrier that the other CTA of the cluster arrives on
 // (cluster-scope acquire).
 __device__ __forceinline__ bool warp_wait_phase_cluster(uint64_t* b, uint32_t parity,
-                                                        volatile int* abort, int code) {
+                                                        volatile int* abort, int code,
+                                                        uint64_t lim) {
   int ok = 1;
   if ((threadIdx.x & 31) == 0) {
     if (!mbar_try_wait_cluster(b, parity)) {
@@ -345,7 +353,7 @@ __device__ __forceinline__ bool warp_wait_phase_cluster(uint64_t* b, uint32_t pa
           ok = 0;
           break;
         }
-        if (gtimer() - t0 > WAIT_LIMIT_NS) {
+        if (gtimer() - t0 > lim) {
           *abort = 1;
           atomicCAS(&g_tc_status, 0, code);
           ok = 0;
@@ -360,10 +368,10 @@ __device__ __forceinline__ bool warp_wait_phase_cluster(uint64_t* b, uint32_t pa
 }
 
 // Drain wait at teardown: bounded, never sets abort.
-__device__ __forceinline__ void drain_phase(uint64_t* b, uint32_t parity) {
+__device__ __forceinline__ void drain_phase(uint64_t* b, uint32_t parity, uint64_t lim) {
   const uint64_t t0 = gtimer();
   while (!mbar_try_wait(b, parity))
-    if (gtimer() - t0 > WAIT_LIMIT_NS / 4) return;
+    if (gtimer() - t0 > lim / 4) return;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -827,12 +835,19 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         const int arow = static_cast<int>(sg.tile * TILE_ROWS) + (SPLIT ? 0 : static_cast<int>(rank) * BM);
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           PROF_T0(t_w);
-          if (!wait_phase(&S.empty[stage], phase ^ 1, abort, 1)) {
+          if (!wait_phase(&S.empty[stage], phase ^ 1, abort, 1, p.wait_ns)) {
             ok = false;
             break;
           }
           PROF_ACC(prof_wait, t_w);
           uint8_t* st = S.ring[stage];
+          if (p.stall) {  // test hook: no copies, so the consumers' waits run out
+            if (++stage == ST) {
+              stage = 0;
+              phase ^= 1;
+            }
+            continue;
+          }
           if constexpr (SPLIT) {  // this CTA's own barrier and bytes
             mbar_expect_tx(&S.full[stage], STAGE_BYTES);
             tma_load_2d(st, &tmA, &S.full[stage], kb * BK, arow);
@@ -862,7 +877,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // flight; the peer stays resident until the teardown cluster barrier
       if (SPLIT || rank == 0)
         for (int s = 0; s < ST; ++s)
-          if (armed[s]) drain_phase(&S.full[s], (armed[s] - 1) & 1);
+          if (armed[s]) drain_phase(&S.full[s], (armed[s] - 1) & 1, p.wait_ns);
       PROF_FLUSH(0, prof_wait);
     }
   } else if (warp == 1) {
@@ -879,15 +894,15 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       for (; ok && seg.next(p, kblocks, n_pairs, sg); ++it) {
         const uint32_t buf = it & 1;
         PROF_T0(t_e);
-        if (SPLIT ? !wait_phase(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2)
-                  : !wait_phase_cluster(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2))
+        if (SPLIT ? !wait_phase(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2, p.wait_ns)
+                  : !wait_phase_cluster(&S.tempty[buf], ((it >> 1) & 1) ^ 1, abort, 2, p.wait_ns))
           break;
         PROF_ACC(prof_tempty, t_e);
         tc_fence_after();
         const uint32_t d = tmem + buf * BUF_COLS;
         for (int kb = sg.kb0; kb < sg.kb1; ++kb) {
           PROF_T0(t_f);
-          if (!wait_phase(&S.full[stage], phase, abort, 3)) {
+          if (!wait_phase(&S.full[stage], phase, abort, 3, p.wait_ns)) {
             ok = false;
             break;
           }
@@ -925,7 +940,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         umma_commit_cta(&S.mma_done);
       else
         umma_commit_pair(&S.mma_done);
-      drain_phase(&S.mma_done, 0);
+      drain_phase(&S.mma_done, 0, p.wait_ns);
       PROF_FLUSH(1, prof_full);
       PROF_FLUSH(2, prof_tempty);
     }
@@ -964,7 +979,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     auto epi_sync = [&]() {
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.epi_sync);
-      const bool ok = warp_wait_phase(&S.epi_sync, eb & 1, abort, 7);
+      const bool ok = warp_wait_phase(&S.epi_sync, eb & 1, abort, 7, p.wait_ns);
       if (ok) mbar_try_wait(&S.epi_sync, eb & 1);  // every lane acquires
       ++eb;
       return ok;
@@ -989,7 +1004,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       for (int i = 0; i < BN / 32; ++i) m[i] = 0u;
       int spill = 0;
       if (live) {
-        const int64_t cur = p.cur_node ? __ldg(p.cur_node + row) : 0;
+        // written by the previous kernel of a search (a PDL predecessor): a
+        // coherent load, never the non-coherent read-only path
+        const int64_t cur = p.cur_node ? ld_relaxed_s64(p.cur_node + row) : 0;
         node_children(p.csr, cur, p.mb, start, count);
         if (cur >= p.idx_lo && cur < p.idx_hi) {
           const uint4* q = reinterpret_cast<const uint4*>(p.masks + (cur - p.idx_lo) * (BN / 32));
@@ -1006,7 +1023,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       PROF_ACC(pe_pro, t_pro);
       PROF_T0(t_wt);
       const uint32_t buf = it & 1;
-      const bool ok = warp_wait_phase(&S.tfull[buf], (it >> 1) & 1, abort, 4);
+      const bool ok = warp_wait_phase(&S.tfull[buf], (it >> 1) & 1, abort, 4, p.wait_ns);
       if (!ok) break;
       // every lane observes the completed phase before touching TMEM
       mbar_try_wait(&S.tfull[buf], (it >> 1) & 1);
@@ -1222,7 +1239,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // of the same rows through shared memory; bounded waits on both sides.
       float (*mg)[32] = S.merge[lg];
       if (half == 1) {
-        if (!warp_wait_phase(&S.merge_empty[lg], (mit & 1) ^ 1, abort, 5)) break;
+        if (!warp_wait_phase(&S.merge_empty[lg], (mit & 1) ^ 1, abort, 5, p.wait_ns)) break;
         mbar_try_wait(&S.merge_empty[lg], (mit & 1) ^ 1);
         put_list([&](int r, float v) { mg[r][lane] = v; });
         warp_arrive(&S.merge_full[lg]);
@@ -1230,7 +1247,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         PROF_ACC(pe_tmem, t_tm);
         continue;
       }
-      if (!warp_wait_phase(&S.merge_full[lg], mit & 1, abort, 6)) break;
+      if (!warp_wait_phase(&S.merge_full[lg], mit & 1, abort, 6, p.wait_ns)) break;
       mbar_try_wait(&S.merge_full[lg], mit & 1);
       absorb(mg);
       warp_arrive(&S.merge_empty[lg]);
@@ -1242,14 +1259,14 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // through distributed shared memory (remote stores, release/acquire
         // at cluster scope on the barriers); CTA 0 writes the outputs.
         if (rank == 1) {
-          if (!warp_wait_phase_cluster(&S.xmerge_empty[lg], (xit & 1) ^ 1, abort, 8)) break;
+          if (!warp_wait_phase_cluster(&S.xmerge_empty[lg], (xit & 1) ^ 1, abort, 8, p.wait_ns)) break;
           put_list([&](int r, float v) { st_cluster_f32(map_to_rank(&S.xm.x[lg][r][lane], 0), v); });
           warp_arrive_cluster(map_to_rank(&S.xmerge_full[lg], 0));
           ++xit;
           PROF_ACC(pe_tmem, t_tm);
           continue;
         }
-        if (!warp_wait_phase_cluster(&S.xmerge_full[lg], xit & 1, abort, 9)) break;
+        if (!warp_wait_phase_cluster(&S.xmerge_full[lg], xit & 1, abort, 9, p.wait_ns)) break;
         absorb(S.xm.x[lg]);
         warp_arrive_cluster(map_to_rank(&S.xmerge_empty[lg], 1));
         ++xit;
@@ -1480,6 +1497,11 @@ bool tc_enabled() {
   return enabled == 1;
 }
 
+// Bound of the tile kernel's waits (ns) and the test hook's pending stalled
+// launches; process-wide, read at each launch.
+static std::atomic<uint64_t> g_wait_limit_ns{tc::WAIT_LIMIT_NS};
+static std::atomic<int> g_stall_launches{0};
+
 int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   using namespace tc;
   auto aligned = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
@@ -1519,6 +1541,12 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.l0_logp = t.l0_logp;
   p.l0_node = t.l0_node;
   p.l0_k = t.l0_k;
+  p.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
+  for (int n = g_stall_launches.load(); n > 0;)
+    if (g_stall_launches.compare_exchange_weak(n, n - 1)) {
+      p.stall = 1;
+      break;
+    }
   // Schedule.  Whole tiles round-robin over the pairs; when the last round
   // would leave pairs idle, the last two rounds' tiles are split into equal
   // k-block ranges instead (at least MIN_SEG k-blocks per pair).
@@ -1613,6 +1641,20 @@ int read_tc_status(int* out, bool reset) {
 }
 
 }  // namespace vtnk
+
+extern "C" int vtnk_set_wait_limit_ns(uint64_t ns) {
+  vtnk::g_wait_limit_ns.store(ns ? ns : vtnk::tc::WAIT_LIMIT_NS);
+  return VTNK_OK;
+}
+
+extern "C" int vtnk_debug_stall_launches(int n) {
+  if (n < 0) {
+    vtnk::set_error("vtnk_debug_stall_launches: n < 0");
+    return VTNK_ERR_ARG;
+  }
+  vtnk::g_stall_launches.store(n);
+  return VTNK_OK;
+}
 
 #ifdef VTNK_TC_PROFILE
 // Tuning builds only: copy (and optionally clear) the phase timers.

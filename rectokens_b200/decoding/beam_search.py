@@ -258,13 +258,16 @@ def constrained_beam_search_from_host(
     config: GenerationConfig,
     bias: Tensor | None = None,
     out: tuple[Tensor, Tensor, Tensor] | None = None,
+    device_out: bool = False,
 ) -> BeamSearchResult:
     """Beam search whose per-level hidden states start in (pinned) host memory.
 
     Level ``l + 1``'s host-to-device copy runs on a side stream while level
     ``l`` computes; the results are copied back into ``out`` (pinned host
     tensors ``(ids (B,k,L), logp (B*k,), node (B*k,))``) when given.  Returns
-    host tensors after synchronising the device.
+    host tensors after synchronising the device, or -- ``device_out`` -- the
+    device tensors, without synchronising (for a caller that gathers them
+    across ranks first).
     """
     dev = weight.device
     main = torch.cuda.current_stream(dev)
@@ -291,6 +294,8 @@ def constrained_beam_search_from_host(
         cand = beam_step(dev_h[l], weight, trie, l, cur, config.beam_size, bias)
         prev_ids, prev_logp, cur, _ = beam_merge(l, B, k, cand, prev_logp, prev_ids)
         dev_h[l] = None
+    if device_out:
+        return BeamSearchResult(prev_ids.view(B, k, Lv), prev_logp, cur)
     if out is None:
         out = (torch.empty((B, k, Lv), dtype=torch.int64, pin_memory=True),
                torch.empty((B * k,), dtype=torch.float32, pin_memory=True),

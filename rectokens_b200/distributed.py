@@ -100,3 +100,48 @@ def gather_results(ids: torch.Tensor, logp: torch.Tensor, node: torch.Tensor, gr
     out[1].view(world, -1).copy_(g_logp)
     out[2].view(world, -1).copy_(g_node)
     return out
+
+
+class ShardFailure(RuntimeError):
+    """A rank's local search failed; raised on every rank of the group."""
+
+
+def checked_gather(rec: ResultRecord, local_error: BaseException | None = None, group=None,
+                   out: torch.Tensor | None = None):
+    """``rec.gather`` preceded by one agreement step, so that a failure on one
+    rank ends the search on every rank instead of leaving the others blocked
+    in the gather: each rank contributes ``rank + 1`` if its local search
+    raised (``local_error``) and 0 otherwise; after a MAX all-reduce every
+    rank raises ``ShardFailure`` naming the highest failing rank, or all
+    proceed to the gather.  A rank that never arrives (it died or hangs) is
+    caught by the process group's timeout, which makes the collective raise
+    on the others.  Costs one small collective; the benchmark's timed search
+    uses the plain gather."""
+    rank = dist.get_rank(group)
+    dev = rec.buf.device
+    flag = torch.tensor([rank + 1 if local_error is not None else 0], dtype=torch.int32,
+                        device=dev)
+    dist.all_reduce(flag, op=dist.ReduceOp.MAX, group=group)
+    failed = int(flag.item())
+    if failed:
+        msg = f"rank {failed - 1} failed before the result gather"
+        if local_error is not None:
+            raise ShardFailure(msg) from local_error
+        raise ShardFailure(msg)
+    return rec.gather(group=group, out=out)
+
+
+def sharded_search(search_fn, n_rows: int, levels: int, device, group=None):
+    """Run ``search_fn() -> (ids (n, L), logp (n,), node (n,))`` on this rank's
+    shard and all-gather every rank's results with ``checked_gather``.
+    Returns the gathered ``(ids (world, n, L), logp (world, n), node (world, n))``."""
+    rec = ResultRecord(n_rows, levels, device)
+    err = None
+    try:
+        ids, logp, node = search_fn()
+        rec.ids.copy_(ids.reshape(n_rows, levels))
+        rec.logp.copy_(logp)
+        rec.node.copy_(node)
+    except Exception as e:  # noqa: BLE001 -- reported to every rank, then re-raised
+        err = e
+    return checked_gather(rec, err, group=group)

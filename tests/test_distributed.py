@@ -88,6 +88,74 @@ def test_sharded_search_equals_single_process():
     np.testing.assert_allclose(g_logp, f_logp, rtol=0, atol=1e-6)
 
 
+def _fault_worker(rank, world, port, mode, q):
+    """One rank of a two-rank search with an injected host-side failure:
+    ``before``  rank 1 raises inside its local search (before the gather);
+    ``after``   rank 1 raises after a successful gather;
+    ``absent``  rank 1 never joins the gather (exits), so rank 0's collective
+                must end by the process group's timeout, not hang."""
+    import datetime
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=5))
+    out = "ok"
+    try:
+        n, levels = 4, 3
+
+        def search():
+            if mode == "before" and rank == 1:
+                raise ValueError("injected failure in the local search")
+            return (torch.full((n, levels), rank, dtype=torch.int64),
+                    torch.full((n,), -1.0 * rank), torch.full((n,), 10 + rank, dtype=torch.int64))
+
+        if mode == "absent" and rank == 1:
+            q.put((rank, "left"))
+            q.close()
+            q.join_thread()  # flush before leaving without any teardown
+            os._exit(0)
+        try:
+            ids, logp, node = D.sharded_search(search, n, levels, "cpu")
+            assert ids.shape == (world, n, levels)
+            assert torch.equal(node[:, 0], torch.tensor([10, 11]))
+            if mode == "after" and rank == 1:
+                raise ValueError("injected failure after the gather")
+        except D.ShardFailure as e:
+            out = f"ShardFailure: {e}"
+        except ValueError as e:
+            out = f"ValueError: {e}"
+        except RuntimeError as e:  # the process group's timeout
+            out = f"RuntimeError: {type(e).__name__}"
+        q.put((rank, out))
+    finally:
+        if mode != "absent":
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["before", "after", "absent"])
+def test_rank_failures_end_the_search(mode):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_fault_worker, args=(r, 2, port, mode, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=90) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+            raise AssertionError("a rank hung")
+    if mode == "before":
+        assert got[0].startswith("ShardFailure: rank 1 failed"), got
+        assert got[1].startswith("ShardFailure: rank 1 failed"), got
+    elif mode == "after":
+        assert got[0] == "ok" and got[1].startswith("ValueError"), got
+    else:
+        assert got[1] == "left"
+        assert got[0].startswith("RuntimeError"), got
+
+
 def test_shard_arithmetic():
     assert D.shard_queries(65536, 3, 8) == (24576, 8192)
     assert D.level_rows(24576, 8192, 0, 10) == (24576, 8192)
