@@ -680,14 +680,17 @@ def op_bench(dev):
     fused_ms = bench(lambda: fused_linear_constrained_node_transition(a, weight.T, cs))
     out["fused_ms"] = round(fused_ms, 4)
     out["fused_ref_published_ms"] = 9.952
-    # full corrected_logits write dominates: B*N*4 bytes + a and the 1,500 W rows
-    out["fused_hbm_frac"] = (B * N * 4 + B * K * 4 + mb * K * 4) / (fused_ms / 1e3) / (
-        _peaks()[0] * 1e9)
+    # full corrected_logits write dominates: B*N*4 bytes + a, the 1,500 W rows
+    # and the [B, max_branches] next_node / valid_idxs tables
+    out["fused_hbm_frac"] = (B * N * 4 + B * K * 4 + mb * K * 4 + B * mb * 16) / (
+        fused_ms / 1e3) / (_peaks()[0] * 1e9)
     logits = a @ weight.T
     mask_ms = bench(lambda: constrained_node_transition(logits, cs))
     route_ms = bench(lambda: constrained_node_transition(a @ weight.T, cs))
     out["mask_only_ms"] = round(mask_ms, 4)
-    out["mask_only_hbm_frac"] = (2 * B * N * 4) / (mask_ms / 1e3) / (_peaks()[0] * 1e9)
+    # the op writes every column and reads only the child columns of the logits
+    out["mask_only_hbm_frac"] = (B * N * 4 + B * mb * 4 + B * mb * 16) / (mask_ms / 1e3) / (
+        _peaks()[0] * 1e9)
     out["mask_route_ms"] = round(route_ms, 4)
     out["mask_route_note"] = "a @ W.T (cuBLAS, fp32) + the mask-only op, as the reference times it"
     out["mask_route_ref_published_ms"] = 814.527

@@ -18,14 +18,18 @@ the whole vocabulary and the CSR trie masks them).  Per level:
   synchronisation per level;
 * KV cache and attention mask are reordered by the parent rows (:305-366).
 
-The ``attr_path`` / ``SparseLinear`` route of the reference passes the weight
-untransposed to the fused op (rectokens/modules/sparse_linear.py:56-94) and is
-not reproduced; use ``rectokens_b200.constrained_beam_search`` for the fused
-hidden-state path.
+Route B, the ``SparseLinear`` output projection (``attr_path``; reference
+:219-237, :281-293): on CSR levels the model's projection runs the fused op
+of ``GenerationConfig.csr_kernel`` -- ``"default"`` (full masked logits, then
+as above), ``"topk"`` (the op's ``beam_size`` best children, scored by the
+log-softmax over those top-k logits only, as the reference does) or
+``"sample"`` (one Gumbel-max sample per row, log-probability 0) -- and its
+``next_nodes`` / ``valid_idxs`` tables give the child nodes.
 """
 
 from __future__ import annotations
 
+import contextlib
 from typing import Optional
 
 import torch
@@ -33,6 +37,8 @@ import torch.nn.functional as F
 from torch import nn
 
 from rectokens_b200 import _lib as L
+from rectokens_b200.modules.constraint_enforcer import SparseTrieConstraintEnforcer
+from rectokens_b200.modules.sparse_linear import SparseLinear
 from rectokens_b200.ops.constrained_node_transition import constrained_node_transition
 from rectokens_b200.schemas.compact_csr_trie import CompactCSRTrie
 from rectokens_b200.schemas.config import GenerationConfig
@@ -90,14 +96,21 @@ def decode_one_step(
         past_key_values, log_probas = gen.past_key_values, gen.log_probas
         attention_mask = gen.attention_mask
 
-    out = model_fwd(input_ids, past_key_values=past_key_values, attention_mask=attention_mask,
-                    use_cache=True)
+    n_dense = len(trie.dense_mask_by_layer)
+    # route B: a SparseLinear output projection runs the fused op on CSR levels
+    sparse = (next((m for m in model_fwd.modules() if isinstance(m, SparseLinear)), None)
+              if isinstance(model_fwd, nn.Module) else None)
+    use_sparse = sparse is not None and step >= n_dense
+    ctx = (sparse.constrained(cs, strategy=config.csr_kernel, temperature=config.temperature,
+                              k=beam_size) if use_sparse else contextlib.nullcontext())
+    with ctx:
+        out = model_fwd(input_ids, past_key_values=past_key_values,
+                        attention_mask=attention_mask, use_cache=True)
     logits = out.logits[:, -1, :]
     new_past = out.past_key_values
     R = logits.shape[0]
     B = R if first else R // k
     prev_ids = None if first else gen.generated_ids.reshape(B * k, -1)
-    n_dense = len(trie.dense_mask_by_layer)
 
     next_nodes = valid_idxs = None
     if step < n_dense:
@@ -107,12 +120,30 @@ def decode_one_step(
         else:
             layer_mask = layer_mask[prev_ids.unbind(-1)]
         masked = logits.float().masked_fill(~layer_mask, float("-inf"))
+    elif use_sparse:
+        next_nodes, valid_idxs = sparse.next_nodes, sparse.valid_idxs
+        masked = logits.float()
     else:
         next_nodes, valid_idxs, masked = constrained_node_transition(logits, cs)
         masked = masked.float()
 
-    lse = torch.logsumexp(masked, dim=-1)
-    if config.temperature == 0.0:
+    routed = use_sparse and (sparse.sample is not None or sparse.topk_idxs is not None)
+    if use_sparse and sparse.sample is not None:
+        # one Gumbel-max sample per row, scored 0 (reference :281-286)
+        cand_tok = sparse.sample.long().unsqueeze(1)
+        cand_logit = torch.where(cand_tok >= 0, 0.0, float("-inf")).float()
+        lse = torch.zeros((R,), dtype=torch.float32, device=logits.device)
+    elif use_sparse and sparse.topk_idxs is not None:
+        # the op's top beam_size children, scored by the log-softmax over
+        # those logits only (reference :287-293)
+        cand_tok = sparse.topk_idxs
+        cand_logit = masked
+        lse = torch.logsumexp(masked, dim=-1)
+    else:
+        lse = torch.logsumexp(masked, dim=-1)
+    if routed:
+        pass  # candidates come from the fused op
+    elif config.temperature == 0.0:
         cand_logit, cand_tok = masked.topk(beam_size, dim=-1)
     else:
         probs = F.softmax(masked / config.temperature, dim=-1)
@@ -133,7 +164,7 @@ def decode_one_step(
     else:
         cand_node = torch.full_like(cand_tok, -1)
 
-    if config.temperature != 0.0:
+    if config.temperature != 0.0 and not routed:
         # the reference scores sampled candidates by log(p_T) (:298-303)
         cand_logit = torch.where(cand_tok >= 0, cand_logit / config.temperature, cand_logit)
         lse = torch.logsumexp(masked / config.temperature, dim=-1)
@@ -171,8 +202,7 @@ def autoregressive_generate(
     """Constrained generation for ``generation_config.steps`` levels; returns
     ``generated_ids`` ``(B, k, steps)`` (reference :140-179)."""
     if attr_path is not None:
-        raise NotImplementedError(
-            "the SparseLinear route is not reproduced; use constrained_beam_search")
+        SparseTrieConstraintEnforcer(attr_path).prepare(model)
     state = ConstrainedGenerationState(
         generation_config=generation_config, generation_state=None,
         constraint_state=ConstraintState(step=0, trie=trie, cur_node=None))

@@ -218,6 +218,12 @@ WORKLOADS: dict[str, Workload] = {
         lambda: catalog_sample_space(4_000_000, 3, 256, seed=0),
         sampling=True, temperature=0.7,
     ),
+    # the SparseLinear route's fixture: every depth has at least beam_size
+    # branches (its top-k op, like torch.topk, needs k <= max_branches)
+    "route_b": Workload(
+        "route_b", 3, 64, 256, "bf16", 64, 5, 5,
+        lambda: catalog_uniform_unique(20_000, 3, 64, seed=1),
+    ),
     "cfg5": Workload(
         "cfg5", 3, 256, 3584, "bf16", 65_536, 10, 10,
         lambda: catalog_density(0.95, 3, 256, seed=0),

@@ -21,6 +21,18 @@ It imports the reference's own Python code and records its outputs:
   The model is a stub whose logits at level ``l`` are ``hidden_l @ W.T`` in
   fp32, with the seeded synthetic hidden states / head of
   ``rectokens_b200.synthetic``.
+* ``search_routeb_route_b.npz`` -- the same search through the reference's
+  ``SparseLinear`` route (``autoregressive_generate(..., attr_path="lm_head")``,
+  ``GenerationConfig.csr_kernel`` "topk" and "default"), whose CSR levels call
+  the fused ops from ``SparseLinear.forward`` (rectokens/modules/
+  sparse_linear.py:47-98) and score candidates as route B of
+  ``decode_one_step`` does (constrained_decoding.py:281-293: for "topk" the
+  log-softmax over the returned top-k logits only).  The stand-in module
+  computes the fused ops with the reference's ``sparse_linear_pytorch``
+  (+ ``torch.topk`` as kernels:816-852).  ``SparseLinear`` passes the weight
+  untransposed where the ops expect ``W.T``; the stand-in takes the operand
+  for what it is (the ``(N, H)`` weight), i.e. the search the route is meant
+  to run.
 * ``philox.npz``    -- ``tl.rand`` and the Gumbel transform of the reference's
   sampling kernel (kernels:359-380) evaluated by Triton's CPU interpreter.
 
@@ -42,7 +54,7 @@ REPO = HERE.parent.parent
 
 
 def _install_kernel_stub():
-    import torch  # noqa: F401
+    import torch
     from rectokens.decoding.vntk import vtnk_pytorch
 
     class _TrieView:
@@ -54,14 +66,34 @@ def _install_kernel_stub():
     def _mask_op(logits, cur_node, row_ptrs, cols_vals, max_branches):
         return vtnk_pytorch(logits, cur_node, _TrieView(row_ptrs, cols_vals, max_branches), 0)
 
+    from rectokens.decoding.vntk import sparse_linear_pytorch
+
+    def _weight(a, b):
+        # SparseLinear hands over the (N, H) weight itself (see the module docstring)
+        return b if b.shape[1] == a.shape[1] else b.T
+
+    def _fused_op(a, b, bias_val, cur_node, row_ptrs, cols_vals, max_branches, has_bias):
+        W = _weight(a, b).float()
+        nn_, vi, cl = sparse_linear_pytorch(a.float(), W, cur_node,
+                                            _TrieView(row_ptrs, cols_vals, max_branches), 0)
+        if has_bias:
+            cl = torch.where(cl > float("-inf"), cl + bias_val.float(), cl)
+        return nn_, vi, cl
+
+    def _topk_op(a, b, bias_val, cur_node, row_ptrs, cols_vals, max_branches, has_bias, k):
+        # kernels:816-852: per-branch logits in a -inf padded [B, mb] buffer,
+        # torch.topk, then valid_idxs.gather
+        nn_, vi, cl = _fused_op(a, b, bias_val, cur_node, row_ptrs, cols_vals, max_branches,
+                                has_bias)
+        branch = torch.where(vi >= 0, cl.gather(1, vi.clamp(min=0)), float("-inf"))
+        tl_, ti = torch.topk(branch, k, dim=-1)
+        return nn_, vi, tl_, vi.gather(1, ti)
+
     stub = types.ModuleType("rectokens.kernels.constrained_node_transition")
     stub._constrained_node_transition_op = _mask_op
-    for name in (
-        "_fused_linear_constrained_node_transition_op",
-        "_fused_linear_constrained_node_transition_sampling_op",
-        "_fused_linear_constrained_node_transition_topk_op",
-    ):
-        setattr(stub, name, None)
+    stub._fused_linear_constrained_node_transition_op = _fused_op
+    stub._fused_linear_constrained_node_transition_topk_op = _topk_op
+    stub._fused_linear_constrained_node_transition_sampling_op = None
     sys.modules["rectokens.kernels.constrained_node_transition"] = stub
 
 
@@ -238,6 +270,61 @@ def search_fixture(out: Path, name: str):
     )
 
 
+class _StubLMHead:
+    """A model whose output projection is an ``nn.Linear`` named ``lm_head``
+    (the SparseLinear route replaces it): level ``l`` feeds ``hidden[l]``
+    through it, one call per level."""
+
+    def __new__(cls, hidden_levels, W):
+        import torch
+        from torch import nn
+
+        class M(nn.Module):
+            def __init__(self):
+                super().__init__()
+                self.lm_head = nn.Linear(W.shape[1], W.shape[0], bias=False)
+                with torch.no_grad():
+                    self.lm_head.weight.copy_(torch.from_numpy(np.asarray(W, np.float32)))
+                self.h = [torch.from_numpy(np.asarray(h, dtype=np.float32))
+                          for h in hidden_levels]
+                self.calls = 0
+
+            def forward(self, input_ids, past_key_values=None, attention_mask=None,
+                        use_cache=True):
+                h = self.h[self.calls]
+                self.calls += 1
+                return types.SimpleNamespace(logits=self.lm_head(h).unsqueeze(1),
+                                             past_key_values=None)
+
+        return M()
+
+
+def routeb_fixture(out: Path, name: str):
+    import torch
+    from rectokens.decoding.constrained_decoding import autoregressive_generate
+    from rectokens.schemas.compact_csr_trie import CompactCSRTrie
+    from rectokens.schemas.config import GenerationConfig
+
+    from rectokens_b200 import synthetic as S
+
+    w = S.WORKLOADS[name]
+    tok = S.to_tokens(w.make_catalog(), w.codes)
+    trie = CompactCSRTrie.from_sorted_batch(torch.from_numpy(tok), vocab_size=w.vocab,
+                                            dense_lookup_layers=1)
+    W = S.bf16_bits_to_f32(S.head_bits(w.seed, w.vocab, w.hidden))
+    hidden = [S.bf16_bits_to_f32(S.hidden_bits(w.seed, l, 0, w.rows(l), w.hidden))
+              for l in range(w.levels)]
+    d = {}
+    for kern in ("topk", "default"):
+        model = _StubLMHead(hidden, W)
+        cfg = GenerationConfig(steps=w.levels, k=w.beams, beam_size=w.topk, temperature=0.0,
+                               csr_kernel=kern)
+        ids = autoregressive_generate(model, trie, torch.zeros(w.batch, 1, dtype=torch.long),
+                                      cfg, attr_path="lm_head")
+        d[f"{kern}/generated_ids"] = ids.numpy()
+    np.savez_compressed(out / f"search_routeb_{name}.npz", **d)
+
+
 def philox_fixture(out: Path):
     code = r'''
 import os, sys
@@ -278,6 +365,7 @@ def main():
     ops_fixtures(HERE)
     for name in ("cfg1", "cfg2"):
         search_fixture(HERE, name)
+    routeb_fixture(HERE, "route_b")
     philox_fixture(HERE)
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)

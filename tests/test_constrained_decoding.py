@@ -116,3 +116,58 @@ def test_log_probas_and_cache_reordering(cuda_ok):
         assert gs.attention_mask.shape == (B * k, 4 + step + 1)
         assert gs.past_key_values[0][0].shape[0] == B * k
         ids = gs.generated_ids.reshape(-1, step + 1)[:, -1:]
+
+
+class _LMHeadModel(nn.Module):
+    """A model whose output projection is ``lm_head`` (an ``nn.Linear``); level
+    ``l`` feeds ``hidden[l]`` through it (the golden fixture's model)."""
+
+    def __init__(self, hidden, W):
+        super().__init__()
+        self.lm_head = nn.Linear(W.shape[1], W.shape[0], bias=False).to(W.device, W.dtype)
+        with torch.no_grad():
+            self.lm_head.weight.copy_(W)
+        self.h = hidden
+        self.calls = 0
+
+    def forward(self, input_ids, past_key_values=None, attention_mask=None, use_cache=True):
+        h = self.h[self.calls]
+        self.calls += 1
+        return types.SimpleNamespace(logits=self.lm_head(h).unsqueeze(1), past_key_values=None)
+
+
+@pytest.mark.parametrize("kern", ["topk", "default"])
+def test_route_b_matches_reference_golden(kern, cuda_ok):
+    """The SparseLinear route (``attr_path="lm_head"``): CSR levels run the
+    fused op of ``csr_kernel`` inside the model's projection; ``topk`` scores
+    candidates by the log-softmax over the op's top-k logits only.  Pinned to
+    the reference's own ``autoregressive_generate`` on the same model."""
+    g = load_golden("search_routeb_route_b.npz")
+    w = S.WORKLOADS["route_b"]
+    dw = WL.make_device_workload(w, DEV)
+    model = _LMHeadModel([h.float() for h in dw.hidden], dw.weight.float())
+    cfg = GenerationConfig(steps=w.levels, k=w.beams, beam_size=w.topk, temperature=0.0,
+                           csr_kernel=kern)
+    ids = autoregressive_generate(model, dw.trie, torch.zeros(w.batch, 1, dtype=torch.long,
+                                                              device=DEV),
+                                  cfg, attr_path="lm_head")
+    np.testing.assert_array_equal(ids.cpu().numpy(), g[f"{kern}/generated_ids"])
+    from rectokens_b200.modules import SparseLinear
+
+    assert isinstance(model.lm_head, SparseLinear)
+
+
+def test_route_b_sampling_paths_are_catalog_items(cuda_ok):
+    """``csr_kernel="sample"`` (k = beam_size = 1): every CSR level draws one
+    Gumbel-max child in the projection; each generated path is an item."""
+    w = S.WORKLOADS["route_b"]
+    codes = w.make_catalog()
+    dw = WL.make_device_workload(w, DEV, trie=WL.build_trie(w, DEV, codes))
+    hidden = [dw.hidden[0]] + [h[::w.beams].contiguous() for h in dw.hidden[1:]]
+    model = _LMHeadModel([h.float() for h in hidden], dw.weight.float())
+    cfg = GenerationConfig(steps=w.levels, k=1, beam_size=1, temperature=0.7, csr_kernel="sample")
+    ids = autoregressive_generate(model, dw.trie, torch.zeros(w.batch, 1, dtype=torch.long,
+                                                              device=DEV),
+                                  cfg, attr_path="lm_head").cpu().numpy().reshape(-1, w.levels)
+    items = {tuple(t) for t in S.to_tokens(codes, w.codes).tolist()}
+    assert all(tuple(r) in items for r in ids.tolist())
