@@ -240,6 +240,35 @@ int vtnk_beam_search(const vtnk_search_t* s, void* workspace, size_t workspace_b
 int vtnk_beam_search_noalloc(const vtnk_search_t* s, int64_t* out_ids, float* out_logp,
                              int64_t* out_node, void* stream);
 
+/* Device CSR trie builder (replaces CompactCSRTrie.from_sorted_batch,
+ * rectokens/schemas/compact_csr_trie.py:97-177, and the catalog sort of
+ * ItemAwareTokenizer.build_item_trie, rectokens/integrations/hf/tokenizer.py:
+ * 198-230): the same row_ptrs / stacked_cols_vals / layer_max_branches /
+ * dense tables, built by sort, scan and segment kernels.  Two phases, because
+ * the output sizes depend on the catalog:
+ *   1. vtnk_trie_count: packs each item's `levels` token ids (each in
+ *      [0, vocab)) into a 64-bit key, radix-sorts the keys unless
+ *      assume_sorted (the reference requires sorted input; duplicates are
+ *      allowed), numbers the nodes in BFS order and writes counts[0] =
+ *      n_nodes (-1 when a token is out of range), counts[1] = nnz and
+ *      counts[2 + d] = nodes at depth d (device int64[levels + 2]).
+ *   2. vtnk_trie_fill (after the caller read the counts and sized the
+ *      outputs): row_ptrs [n_nodes], cols_vals [2, nnz + 1] (with the -1
+ *      sentinel column), layer_max_branches [levels] (device int64), and for
+ *      dense_layers > 0 the prefix masks dense_masks[d] (vocab^(d+1) bytes
+ *      of 0/1) and dense_states (vocab^dense_layers int64).
+ * Both read and write the caller's workspace (vtnk_trie_workspace_bytes);
+ * nothing is allocated.  Requires levels * bits(vocab - 1) <= 64 and
+ * n_items * levels < 2^31. */
+size_t vtnk_trie_workspace_bytes(int64_t n_items, int64_t levels);
+int vtnk_trie_count(const int64_t* sem_ids, int64_t n_items, int64_t levels, int64_t vocab,
+                    int assume_sorted, void* workspace, size_t workspace_bytes, int64_t* counts,
+                    void* stream);
+int vtnk_trie_fill(int64_t n_items, int64_t levels, int64_t vocab, int64_t dense_layers,
+                   void* workspace, size_t workspace_bytes, int64_t n_nodes, int64_t nnz,
+                   int64_t* row_ptrs, int64_t* cols_vals, int64_t* layer_max_branches,
+                   uint8_t* const* dense_masks, int64_t* dense_states, void* stream);
+
 /* Synthetic hidden states (benchmark / test input generator, no reference
  * counterpart): out[r, h] = table[mix64(key(seed, stream_id) ^ ((row0 + r) * H + h)) >> 48]
  * with the 65,536-entry quantile table given as bf16 bits (dtype BF16) or fp32

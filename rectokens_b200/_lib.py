@@ -12,7 +12,11 @@ from pathlib import Path
 
 import torch
 
-LIB_PATH = Path(__file__).resolve().with_name("libvtnk_b200.so")
+import os
+
+# VTNK_LIB_PATH: load another build of the library (tuning builds)
+LIB_PATH = Path(os.environ.get("VTNK_LIB_PATH") or
+                Path(__file__).resolve().with_name("libvtnk_b200.so"))
 
 F32, BF16, F16 = 0, 1, 2
 DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
@@ -32,6 +36,9 @@ EXPORTS = (
     "vtnk_beam_search",
     "vtnk_beam_search_noalloc",
     "vtnk_synth_normal",
+    "vtnk_trie_workspace_bytes",
+    "vtnk_trie_count",
+    "vtnk_trie_fill",
     "vtnk_device_status",
     "vtnk_set_wait_limit_ns",
     "vtnk_debug_stall_launches",
@@ -99,11 +106,16 @@ def lib() -> ctypes.CDLL:
             "vtnk_beam_search": [POINTER(Search), P, c_size_t, P, P, P, V],
             "vtnk_beam_search_noalloc": [POINTER(Search), P, P, P, V],
             "vtnk_synth_normal": [c_uint64, c_uint64, I64, I64, I64, P, c_int32, P, V],
+            "vtnk_trie_count": [P, I64, I64, I64, c_int, P, c_size_t, P, V],
+            "vtnk_trie_fill": [I64, I64, I64, I64, P, c_size_t, I64, I64, P, P, P,
+                               POINTER(c_void_p), P, V],
         }
         for name, args in sig.items():
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = c_int
+        L.vtnk_trie_workspace_bytes.argtypes = [I64, I64]
+        L.vtnk_trie_workspace_bytes.restype = c_size_t
         L.vtnk_beam_search_workspace_bytes.argtypes = [POINTER(Search)]
         L.vtnk_beam_search_workspace_bytes.restype = c_size_t
         L.vtnk_set_wait_limit_ns.argtypes = [c_uint64]

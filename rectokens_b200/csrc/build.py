@@ -43,10 +43,15 @@ def _stale(obj: Path, src: Path) -> bool:
     return obj.stat().st_mtime < max(d.stat().st_mtime for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None) -> Path:
-    BUILD.mkdir(exist_ok=True)
+def build(force: bool = False, verbose: bool = False, extra: list[str] | None = None,
+          out: Path | None = None, build_dir: Path | None = None) -> Path:
+    """Compile (stale objects only) and link; ``out`` / ``build_dir`` place a
+    tuning build elsewhere."""
+    lib = Path(out) if out else LIB
+    bdir = Path(build_dir) if build_dir else BUILD
+    bdir.mkdir(parents=True, exist_ok=True)
     srcs = sorted(CSRC.glob("*.cu"))
-    objs = [BUILD / (s.stem + ".o") for s in srcs]
+    objs = [bdir / (s.stem + ".o") for s in srcs]
     todo = [(s, o) for s, o in zip(srcs, objs) if force or _stale(o, s)]
     cc = nvcc()
 
@@ -65,12 +70,12 @@ def build(force: bool = False, verbose: bool = False, extra: list[str] | None = 
 
     with cf.ThreadPoolExecutor(max_workers=min(8, max(1, len(todo)))) as ex:
         list(ex.map(compile_one, todo))
-    if todo or not LIB.exists() or force:
-        cmd = [cc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(LIB)]
+    if todo or not lib.exists() or force:
+        cmd = [cc, *ARCH, "-shared", "-Xcompiler", "-fPIC", *map(str, objs), "-o", str(lib)]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":

@@ -214,7 +214,9 @@ __device__ __forceinline__ bool wait_phase(uint64_t* b, uint32_t parity, volatil
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
   for (uint32_t i = 1;; ++i) {
+#ifndef VTNK_TC_SPIN
     if (ns) __nanosleep(ns);  // back off so a waiting role does not steal issue slots
+#endif
     if (mbar_try_wait(b, parity)) return true;
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
@@ -265,7 +267,9 @@ __device__ __forceinline__ bool wait_phase_cluster(uint64_t* b, uint32_t parity,
   const uint64_t t0 = gtimer();
   uint32_t ns = 0;
   for (uint32_t i = 1;; ++i) {
+#ifndef VTNK_TC_SPIN
     if (ns) __nanosleep(ns);
+#endif
     if (mbar_try_wait_cluster(b, parity)) return true;
     if (i >= 4) ns = ns ? (ns < 128 ? ns * 2 : ns) : 16;
     if ((i & 15) == 0) {
@@ -865,6 +869,15 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             tma_load_2d_pair(st + A_BYTES, &tmW, lbar, kb * BK, wrow);
 #endif
           }
+#ifdef VTNK_TC_PREFETCH
+          // tuning option: pull this tile's A k-block VTNK_TC_PREFETCH stages
+          // ahead into L2, so its copy later hits L2
+          if (kb + VTNK_TC_PREFETCH < sg.kb1)
+            asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(
+                             reinterpret_cast<uint64_t>(&tmA)),
+                         "r"((kb + VTNK_TC_PREFETCH) * BK), "r"(arow)
+                         : "memory");
+#endif
           if (armed[stage] == 0 && stage == 0) TRACE(2);
           ++armed[stage];
           if (++stage == ST) {

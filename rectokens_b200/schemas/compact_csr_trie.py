@@ -95,14 +95,18 @@ class CompactCSRTrie(NamedTuple):
     ) -> "CompactCSRTrie":
         """Vectorised build from lexicographically sorted codes ``(n_items, L)``.
 
-        Follows reference compact_csr_trie.py:97-177.  Works on any device;
-        the only host synchronisations are the per-depth branch maxima.
+        Follows reference compact_csr_trie.py:97-177.  On a CUDA device the
+        build runs in the library's trie kernels (scan / segment; two host
+        synchronisations, for the output sizes and the branch maxima); on the
+        CPU it runs as tensor operations.
 
         Node numbering: a (depth, item) pair opens a new node when the item's
         prefix up to that depth differs from the previous item's.  New nodes are
         numbered depth-major, item-minor, starting at 1 (root = 0), which is
         exactly BFS order for a sorted catalog.
         """
+        if sem_ids.is_cuda and _device_buildable(sem_ids, vocab_size, dense_lookup_layers):
+            return _build_on_device(sem_ids, vocab_size, dense_lookup_layers, assume_sorted=True)
         n_items, L = sem_ids.shape
         dense_lookup_layers = min(dense_lookup_layers, L)
         dev = sem_ids.device
@@ -163,6 +167,23 @@ class CompactCSRTrie(NamedTuple):
             vocab_size=vocab_size,
         )
 
+    @classmethod
+    def from_codes(
+        cls, sem_ids: Tensor, vocab_size: int, dense_lookup_layers: int = 2
+    ) -> "CompactCSRTrie":
+        """Build from item token rows in any order (duplicates allowed): the
+        lexicographic sort of ``ItemAwareTokenizer.build_item_trie``
+        (rectokens/integrations/hf/tokenizer.py:214-229) followed by
+        ``from_sorted_batch``.  On a CUDA device the sort is the library's
+        radix sort of packed keys."""
+        if sem_ids.is_cuda and _device_buildable(sem_ids, vocab_size, dense_lookup_layers):
+            return _build_on_device(sem_ids, vocab_size, dense_lookup_layers, assume_sorted=False)
+        rows = sem_ids.to(torch.long)
+        order = torch.arange(rows.shape[0], device=rows.device)
+        for d in range(rows.shape[1] - 1, -1, -1):  # stable passes, last level first
+            order = order[torch.sort(rows[order, d], stable=True).indices]
+        return cls.from_sorted_batch(rows[order], vocab_size, dense_lookup_layers)
+
     # ------------------------------------------------------------------ helpers
     def to(self, device) -> "CompactCSRTrie":
         """Copy every tensor field to ``device``."""
@@ -184,3 +205,56 @@ def _dense_masks(full_mask: Tensor, layers: int) -> list[Tensor]:
         m = m.any(dim=-1)
     out.reverse()
     return out
+
+
+def _device_buildable(sem_ids: Tensor, vocab_size: int, dense_lookup_layers: int) -> bool:
+    """Whether the library's trie kernels take this catalog: every item's
+    tokens pack into one 64-bit key and node ids fit in 32 bits."""
+    n, L = sem_ids.shape
+    bits = max(1, (max(vocab_size, 2) - 1).bit_length())
+    return (1 <= L <= 16 and bits * L <= 64 and bits <= 62 and n * L < 2**31 - 2
+            and min(dense_lookup_layers, L) <= 4)
+
+
+def _build_on_device(sem_ids: Tensor, vocab_size: int, dense_lookup_layers: int,
+                     assume_sorted: bool) -> "CompactCSRTrie":
+    """The trie kernels of libvtnk_b200 (``vtnk_trie_count`` + ``vtnk_trie_fill``)."""
+    import ctypes
+
+    from rectokens_b200 import _lib as L
+
+    lib = L.lib()
+    dev = sem_ids.device
+    n, levels = sem_ids.shape
+    dl = min(dense_lookup_layers, levels)
+    sem = sem_ids.to(torch.long).contiguous()
+    ws = torch.empty((lib.vtnk_trie_workspace_bytes(n, levels),), dtype=torch.uint8, device=dev)
+    counts = torch.empty((levels + 2,), dtype=torch.long, device=dev)
+    stream = L.stream_of(dev)
+    L.check(lib.vtnk_trie_count(sem.data_ptr() if n else None, n, levels, vocab_size,
+                                int(assume_sorted), ws.data_ptr(), ws.numel(),
+                                counts.data_ptr(), stream))
+    c = counts.tolist()  # output sizes
+    if c[0] < 0:
+        raise ValueError(f"token ids must lie in [0, vocab_size={vocab_size})")
+    n_nodes, nnz = c[0], c[1]
+    row_ptrs = torch.empty((n_nodes,), dtype=torch.long, device=dev)
+    cols_vals = torch.empty((2, nnz + 1), dtype=torch.long, device=dev)
+    lmb = torch.empty((levels,), dtype=torch.long, device=dev)
+    masks = [torch.empty((vocab_size,) * (d + 1), dtype=torch.bool, device=dev)
+             for d in range(dl)]
+    states = torch.empty((vocab_size,) * dl, dtype=torch.long, device=dev)
+    mp = (ctypes.c_void_p * max(1, dl))(*[m.data_ptr() for m in masks])
+    L.check(lib.vtnk_trie_fill(n, levels, vocab_size, dl, ws.data_ptr(), ws.numel(), n_nodes,
+                               nnz, row_ptrs.data_ptr(), cols_vals.data_ptr(), lmb.data_ptr(),
+                               mp, states.data_ptr() if dl else None, stream))
+    if dl == 0:
+        states.zero_()
+    return CompactCSRTrie(
+        row_ptrs=row_ptrs,
+        stacked_cols_vals=cols_vals,
+        layer_max_branches=lmb.tolist(),
+        dense_mask_by_layer=masks,
+        dense_states=states,
+        vocab_size=vocab_size,
+    )

@@ -106,3 +106,14 @@ def test_depth_layout_cache_follows_the_trie():
     del csr
     gc.collect()
     assert len(B._LAYOUT_CACHE) == n - 1                     # dropped with the trie
+
+
+@pytest.mark.parametrize("name", case_names(TRIE))
+def test_from_codes_sorts_like_the_tokenizer(name):
+    """``from_codes`` (any row order, duplicates allowed) equals the sorted
+    build, as ``ItemAwareTokenizer.build_item_trie`` sorts before building."""
+    d = group(TRIE, name + "/")
+    rows = np.concatenate([d["sem_ids"], d["sem_ids"][::2]])
+    rows = rows[np.random.default_rng(2).permutation(rows.shape[0])]
+    csr = CompactCSRTrie.from_codes(torch.from_numpy(rows), int(d["vocab"]), int(d["dl"]))
+    _check(csr, group(d, "sorted/"))
