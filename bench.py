@@ -53,10 +53,11 @@ UNIT = "seq*beams/s"
 
 # Fixed CPU-baseline samples (queries, all levels) per workload.
 CPU_QUERIES = {"cfg1": 4, "cfg2": 64, "cfg3": 16, "cfg4": 256, "cfg5": 64}
-# DRAM bytes per hidden-state row of the step kernel, per level, from the
-# committed small-case ncu captures (profiles/tc_beam_step_cfg5.md); scaled by
-# the rows of a full-size launch.
-TRAFFIC_PER_ROW = {"cfg5": (7460.0, 7460.0, 7460.0)}
+# DRAM bytes (read + write) per hidden-state row of the step kernel, per
+# level, from the committed small-case ncu capture of all three levels
+# (profiles/tc_beam_step_cfg5.md: batch 8192, dram__bytes_read/write.sum);
+# scaled by the rows of a full-size launch.
+TRAFFIC_PER_ROW = {"cfg5": (7468.3, 7424.3, 7514.1)}
 
 
 def _peaks():
@@ -506,8 +507,9 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     tpr = TRAFFIC_PER_ROW.get(name)
     roof["traffic"] = (round(sum(tpr[l] * rows_l[l] for l in range(w.levels)))
                        if tpr and len(tpr) >= w.levels else None)
-    roof["traffic_note"] = ("per-level DRAM bytes per row from small-case ncu captures "
-                            "(profiles/tc_beam_step_cfg5.md), scaled by this search's rows")
+    roof["traffic_note"] = ("per-level DRAM bytes per row from a small-case ncu capture of "
+                            "all three levels (profiles/tc_beam_step_cfg5.md), scaled by "
+                            "this search's rows")
     roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json burst figures)"
     roof["kernel"] = "vtnk beam-step kernel, all levels of one search"
     roof["tensor_frac"] = (tot_flops / t_step / 1e12) / tc_peak

@@ -1176,6 +1176,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float* sx = &S.chunk_x[warp - 2][0][0];
 #pragma unroll 1
         for (int ci = 0; ci < NCW; ++ci) {
+#ifdef VTNK_TC_EXPERIMENT_NOPASS2
+          break;  // tuning experiment only: pass 1 alone
+#endif
           if (!__any_sync(0xffffffffu, cmax[ci] >= lb && cmax[ci] > -INFINITY)) continue;
           const int chunk = c0 + ci;
           float x[32];
@@ -1333,6 +1336,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             node = (edge_ids && !by_slot) ? start + slot + 1 : __ldg(p.csr.vals + start + slot);
             lv = top.v[j];
           }
+#ifdef VTNK_TC_EXPERIMENT_NOOUT
+          if (lv != 12345.f) continue;  // tuning experiment only: outputs (almost) never stored
+#endif
           if (p.cand_tok) p.cand_tok[o + j] = tok;
           if (p.cand_logit) p.cand_logit[o + j] = lv;  // sampling: the winning score
           if (p.cand_node) p.cand_node[o + j] = node;
