@@ -103,7 +103,9 @@ template <bool SPLIT>
 struct SharedT {
   static constexpr int ST = SPLIT ? STAGES - 1 : STAGES;
   uint8_t ring[ST][STAGE_BYTES];  // 1024-aligned stages
-  float chunk_x[EPI_WARPS][32][32];    // epilogue: one 32-column chunk per warp, [col][lane]
+  float chunk_x[EPI_WARPS][32][32];    // epilogue, per warp, [slot][lane]: top-n candidate
+                                       // values (sampling: one 32-column chunk)
+  uint8_t chunk_c[EPI_WARPS][32][32];  // their window columns
   float merge[4][MAX_NC + MAX_NC / 4 + 2][32];  // upper-half -> lower-half partial results:
                                                 // NC values, NC byte-packed columns, max, sum
   XMerge<SPLIT> xm;  // split: window half 1 -> half 0 (empty in the pair variant)
@@ -172,6 +174,13 @@ struct Params {
 };
 
 // ------------------------------------------------------------------ PTX wrappers
+constexpr float kLog2e = 1.4426950408889634f;
+// 2^x by the SFU's base-2 exponential (PTX ex2.approx.ftz.f32).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 __device__ __forceinline__ uint32_t su32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -1160,7 +1169,11 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           mx = nm;
           float e[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) e[i] = (x[i] > -INFINITY) ? __expf(x[i] - mx) : 0.f;
+          // exp(x - mx) = 2^(x log2e - mx log2e): one FFMA and one ex2 per value
+          // (a -inf value gives 2^-inf = 0)
+          const float nmx = mx > -INFINITY ? -mx * kLog2e : 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) e[i] = ex2_approx(fmaf(x[i], kLog2e, nmx));
 #pragma unroll
           for (int w = 16; w >= 1; w >>= 1)
 #pragma unroll
@@ -1169,11 +1182,31 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         if (warp == 2 && lane == 0 && it == 0) TRACE(8);
       const float lb = nth_largest<G, NC>(gm);
-        // Pass 2: top-n in column order over the values >= lb.  Each lane
-        // inserts only its values above its current n-th best; the warp loops
-        // max-over-lanes(candidates) times.  Values are read back from shared
-        // memory ([col][lane]: conflict-free for any per-lane column).
-        float* sx = &S.chunk_x[warp - 2][0][0];
+        // Pass 2: the values >= lb of each lane, in column order, are appended
+        // to the lane's candidate list in shared memory ([slot][lane], value
+        // and window column); the list is then inserted into the top-n.  The
+        // warp's insert loop runs max-over-lanes(list length) times once per
+        // tile instead of once per chunk; a list that could overflow its 32
+        // slots is inserted early.
+        float* sv = &S.chunk_x[warp - 2][0][0];
+        uint8_t* sc = &S.chunk_c[warp - 2][0][0];
+        int cnt = 0;
+        auto flush = [&]() {
+          const int n = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(cnt)));
+          __syncwarp();
+          float ynext = cnt > 0 ? sv[lane] : -INFINITY;
+          int cnext = sc[lane];
+#pragma unroll 1
+          for (int j = 0; j < n; ++j) {  // software-pipelined: next read overlaps the insert
+            const float y = ynext;
+            const int col = cnext;
+            ynext = j + 1 < cnt ? sv[(j + 1) * 32 + lane] : -INFINITY;
+            cnext = sc[((j + 1) & 31) * 32 + lane];
+            top.insert(y, col);  // no-op for -inf / values not above the n-th best
+          }
+          cnt = 0;
+          __syncwarp();
+        };
 #pragma unroll 1
         for (int ci = 0; ci < NCW; ++ci) {
 #ifdef VTNK_TC_EXPERIMENT_NOPASS2
@@ -1183,32 +1216,23 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const int chunk = c0 + ci;
           float x[32];
           load_chunk(taddr, chunk, m, has_bias, S.bias, x);
-          const float thr = top.v[NC - 1];
           uint32_t pend = 0;
-          __syncwarp();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            pend |= (x[i] > thr && x[i] >= lb) ? (1u << i) : 0u;
-            sx[i * 32 + lane] = x[i];
-          }
-          __syncwarp();
+          for (int i = 0; i < 32; ++i) pend |= (x[i] >= lb && x[i] > -INFINITY) ? (1u << i) : 0u;
 #ifdef VTNK_TC_EXPERIMENT_NOSELECT
           pend = 0u;  // tuning experiment only: measures the pipeline without top-n work
 #endif
-          // software-pipelined: the next candidate's shared-memory read overlaps
-          // the current insert
-          int inext = pend ? __ffs(pend) - 1 : -1;
-          pend &= pend - 1;
-          float ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
-          while (__any_sync(0xffffffffu, inext >= 0)) {
-            const float y = ynext;
-            const int col = chunk * 32 + inext;
-            inext = pend ? __ffs(pend) - 1 : -1;
-            pend &= pend - 1;
-            ynext = inext >= 0 ? sx[inext * 32 + lane] : -INFINITY;
-            top.insert(y, col);  // no-op for -inf / values no longer above the n-th best
+          if (__any_sync(0xffffffffu, cnt + __popc(pend) > 32)) flush();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            if ((pend >> i) & 1u) {
+              sv[cnt * 32 + lane] = x[i];
+              sc[cnt * 32 + lane] = static_cast<uint8_t>(chunk * 32 + i);
+              ++cnt;
+            }
           }
         }
+        flush();
       }
       __syncwarp();
       release_acc(buf);
@@ -1242,13 +1266,35 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) +
               (omx > -INFINITY ? osum * __expf(omx - nm) : 0.f);
         mx = nm;
+        // Two sorted lists, ours with the lower columns: a two-pointer merge
+        // through shared memory (our list goes to this warp's candidate
+        // slots), ties to ours, i.e. to the lower column.
+        float* ov = &S.chunk_x[warp - 2][0][0];
+        uint8_t* oc = &S.chunk_c[warp - 2][0][0];
+        __syncwarp();
 #pragma unroll
         for (int j = 0; j < NC; ++j) {
-          const float y = src[j][lane];
-          const uint32_t cb = (__float_as_uint(src[MAX_NC + j / 4][lane]) >> (8 * (j & 3))) & 0xFFu;
-          const int c = (y > -INFINITY) ? static_cast<int>(cb) : -1;  // column 255 packs as 0xFF too
-          if (__any_sync(0xffffffffu, y > top.v[NC - 1])) top.insert(y, c);
+          ov[j * 32 + lane] = top.v[j];
+          oc[j * 32 + lane] = static_cast<uint8_t>(top.c[j] & 0xFF);
         }
+        __syncwarp();
+        int ia = 0, ib = 0;
+#pragma unroll
+        for (int j = 0; j < NC; ++j) {
+          const float va = ia < NC ? ov[ia * 32 + lane] : -INFINITY;
+          const int ca = oc[(ia < NC ? ia : 0) * 32 + lane];
+          const int ibc = ib < NC ? ib : 0;
+          const float vb = ib < NC ? src[ibc][lane] : -INFINITY;
+          const int cb = static_cast<int>(
+              (__float_as_uint(src[MAX_NC + ibc / 4][lane]) >> (8 * (ibc & 3))) & 0xFFu);
+          const bool take_a = !(vb > va);
+          const float v = take_a ? va : vb;
+          top.v[j] = v;
+          top.c[j] = v > -INFINITY ? (take_a ? ca : cb) : -1;
+          ia += take_a ? 1 : 0;
+          ib += take_a ? 0 : 1;
+        }
+        __syncwarp();
       };
 
       // The upper-half warp hands its partial result to the lower-half warp
