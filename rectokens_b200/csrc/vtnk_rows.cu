@@ -427,25 +427,38 @@ template <int G>
 __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm, int64_t q0,
                                                   int n, int L, int per_q) {
   constexpr int QPB = 128 / G;
+  const int g = threadIdx.x / G;        // query slot in the block
+  const int li = threadIdx.x % G;       // list (parent) index
+  const int64_t b = q0 + g;
+  const int64_t row0 = p.level == 0 ? b : b * p.k;
+  const bool has = li < L && b < p.B;
+  // the list's previous log-prob and log-sum-exp, loaded before (and in
+  // flight with) the staging loads
+  const float pv = (has && p.level > 0) ? p.prev_logp[row0 + li] : 0.f;
+  const float ls = has ? p.row_lse[row0 + li] : 0.f;
   __syncthreads();  // the previous block's readers are done with gsm
   {
     const int64_t nq64 = p.B - q0 < QPB ? p.B - q0 : QPB;
     const int total = static_cast<int>(nq64) * per_q;
     const int64_t e0 = q0 * per_q;
-    for (int t = threadIdx.x; t < total; t += 128)
-      gsm[t] = p.cand_logit[e0 + t];  // -inf: a missing candidate
+    // all of a thread's loads issued before its stores: one memory latency
+    constexpr int U = 8;
+    for (int t0 = threadIdx.x; t0 < total; t0 += 128 * U) {
+      float v[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        const int t = t0 + j * 128;
+        v[j] = t < total ? p.cand_logit[e0 + t] : 0.f;  // -inf: a missing candidate
+      }
+#pragma unroll
+      for (int j = 0; j < U; ++j)
+        if (t0 + j * 128 < total) gsm[t0 + j * 128] = v[j];
+    }
   }
   __syncthreads();
-  const int g = threadIdx.x / G;        // query slot in the block
-  const int li = threadIdx.x % G;       // list (parent) index
-  const int64_t b = q0 + g;
   if (b >= p.B) return;                 // whole groups retire together (the last block)
   const unsigned gmask = (G == 32) ? 0xffffffffu : (0xffffu << ((threadIdx.x & 31) & 16));
   const float* my = gsm + g * per_q;
-  const int64_t row0 = p.level == 0 ? b : b * p.k;
-  const bool has = li < L;
-  const float pv = (has && p.level > 0) ? p.prev_logp[row0 + li] : 0.f;
-  const float ls = has ? p.row_lse[row0 + li] : 0.f;
   bool ok = true;
   if (has)
     for (int j = 1; j < n; ++j) ok = ok && !(my[li * n + j] > my[li * n + j - 1]);
@@ -519,11 +532,21 @@ __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm
   const int64_t parent = row0 + bi;
   const int64_t e = parent * n + (my_c - bi * n);
   const int64_t o = b * p.k + r;
+  // every load of the outputs issued before the first store
+  const int64_t node = p.cand_node[e];
+  const int64_t tok = p.cand_tok[e];
+  constexpr int HB = 8;
+  int64_t hist[HB];
+#pragma unroll
+  for (int t = 0; t < HB; ++t) hist[t] = t < p.level ? p.prev_ids[parent * p.level + t] : 0;
   p.out_logp[o] = my_v;
-  p.out_node[o] = p.cand_node[e];
+  p.out_node[o] = node;
   p.out_parent[o] = parent;
-  p.out_ids[o * (p.level + 1) + p.level] = p.cand_tok[e];
-  for (int t = 0; t < p.level; ++t)
+  p.out_ids[o * (p.level + 1) + p.level] = tok;
+#pragma unroll
+  for (int t = 0; t < HB; ++t)
+    if (t < p.level) p.out_ids[o * (p.level + 1) + t] = hist[t];
+  for (int t = HB; t < p.level; ++t)
     p.out_ids[o * (p.level + 1) + t] = p.prev_ids[parent * p.level + t];
 }
 
