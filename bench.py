@@ -5,7 +5,8 @@
 A step = one full L-level constrained beam search over this rank's shard of
 the workload (config 5 by default: 16M-item catalog, H=3584, bf16, batch
 65,536 x 10 beams, top-k 10; `--workload cfg4` is the Gumbel-max sampled
-search), plus -- for N > 1 -- the NCCL all-gather of every rank's results.
+search), plus -- for N > 1 -- the all-gather of every rank's results (over
+peer memory by default: one push + flag-barrier kernel; `--gather nccl`).
 Inputs (trie, head rows, per-level hidden states) are resident in HBM before
 timing.  One search is captured as a CUDA graph and replayed K times after W
 warm-ups, timed with CUDA events on the launching stream.  At config 5 the
@@ -336,6 +337,19 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     rec = ResultRecord(Bq * k, w.levels, dev)
     gather_buf = (torch.empty((world * rec.nbytes,), dtype=torch.uint8, device=dev)
                   if world > 1 else None)
+    # N > 1: the results' all-gather -- over peer memory (one push + flag
+    # barrier kernel, int32 ids / nodes) or NCCL (--gather nccl)
+    pgather = None
+    if world > 1 and not w.sampling and args.gather == "peer":
+        from rectokens_b200.distributed import PeerGather
+
+        pgather = PeerGather(Bq * k, w.levels, dev)
+
+    def do_gather():
+        if pgather is not None:
+            pgather.push(rec.ids, rec.logp, rec.node)
+        else:
+            rec.gather(out=gather_buf)
 
     temp_t = torch.tensor([w.temperature], dtype=torch.float32, device=dev)
     samp_out = [(torch.empty((R,), dtype=torch.float32, device=dev),
@@ -406,7 +420,7 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
             time.sleep(0.3)
         one_search()
         if world > 1 and not w.sampling:
-            rec.gather(out=gather_buf)
+            do_gather()
     torch.cuda.synchronize(dev)
     if w.sampling:
         curs = [None] + [samp_out[l][1].clone() for l in range(w.levels - 1)]
@@ -466,7 +480,7 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
             fev[s_][1].record(stream)
         g_search.replay()
         if world > 1 and not w.sampling:
-            rec.gather(out=gather_buf)
+            do_gather()
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -483,7 +497,7 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     gather_ms = None
     if world > 1 and not w.sampling:
         dist.barrier()
-        gather_ms = replay_timed(lambda: rec.gather(out=gather_buf), n_lvl)
+        gather_ms = replay_timed(do_gather, n_lvl)
     t = torch.tensor([ms_total, search_ms, gather_ms or 0.0], dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -526,6 +540,7 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     roof["roofline_ms"] = round(max(t_hbm, t_tc) * 1e3, 4)
     breakdown = {"search_ms": round(float(t[1].item()), 4),
                  "gather_ms": round(float(t[2].item()), 4) if gather_ms is not None else None,
+                 "gather": args.gather if world > 1 else None,
                  "step_ms": [round(x, 4) for x in lvl_ms],
                  "merge_ms": [round(x, 4) for x in merge_ms[1:]] if not w.sampling else []}
 
@@ -534,7 +549,13 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     if not args.no_parity:
         torch.cuda.synchronize(dev)
         if world > 1 and not w.sampling:
-            g_ids, g_logp, g_node = rec.gather(out=gather_buf)
+            if pgather is not None:
+                do_gather()
+                g_ids, g_logp, g_node, pstatus = pgather.result()
+                if pstatus:
+                    raise RuntimeError(f"peer gather status {pstatus}")
+            else:
+                g_ids, g_logp, g_node = rec.gather(out=gather_buf)
             all_ids = g_ids.reshape(w.batch, k, w.levels).cpu().numpy()
             all_logp = g_logp.reshape(-1).cpu().numpy()
             all_node = g_node.reshape(-1).cpu().numpy()
@@ -596,19 +617,32 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
         else:
             # the search on this rank's shard, its results packed and
             # all-gathered, the gathered results read back by rank 0
-            outs = (torch.empty((world * rec.nbytes,), dtype=torch.uint8, pin_memory=True),)
             e2e_rec = ResultRecord(Bq * k, w.levels, dev)
-            e2e_gather = torch.empty_like(gather_buf)
+            if pgather is not None:
+                outs = (torch.empty((world, Bq * k, w.levels), dtype=torch.int32,
+                                    pin_memory=True),
+                        torch.empty((world, Bq * k), dtype=torch.float32, pin_memory=True),
+                        torch.empty((world, Bq * k), dtype=torch.int32, pin_memory=True))
+            else:
+                outs = (torch.empty((world * rec.nbytes,), dtype=torch.uint8, pin_memory=True),)
+                e2e_gather = torch.empty_like(gather_buf)
 
             def e2e_call():
                 r = constrained_beam_search_from_host(host, dw.weight, dw.trie, cfg,
                                                       device_out=True)
-                e2e_rec.ids.copy_(r.generated_ids.view(Bq * k, w.levels))
-                e2e_rec.logp.copy_(r.log_probas)
-                e2e_rec.node.copy_(r.cur_node)
-                e2e_rec.gather(out=e2e_gather)
-                if rank == 0:
-                    outs[0].copy_(e2e_gather, non_blocking=True)
+                if pgather is not None:
+                    pgather.push(r.generated_ids.view(Bq * k, w.levels), r.log_probas,
+                                 r.cur_node)
+                    if rank == 0:
+                        for o, x in zip(outs, pgather.result()[:3]):
+                            o.copy_(x, non_blocking=True)
+                else:
+                    e2e_rec.ids.copy_(r.generated_ids.view(Bq * k, w.levels))
+                    e2e_rec.logp.copy_(r.log_probas)
+                    e2e_rec.node.copy_(r.cur_node)
+                    e2e_rec.gather(out=e2e_gather)
+                    if rank == 0:
+                        outs[0].copy_(e2e_gather, non_blocking=True)
                 torch.cuda.current_stream(dev).synchronize()
         e2e_call()
         if world > 1:
@@ -629,7 +663,7 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
                "ms_per_step": float(te.item()),
                "path": ("public API: constrained_beam_search_from_host per level (H2D of level "
                         "l+1 overlapped with level l), " +
-                        ("results all-gathered over NCCL and read back by rank 0"
+                        (f"results all-gathered ({args.gather}) and read back by rank 0"
                          if world > 1 else "results read back to pinned host memory"))}
         del host
 
@@ -731,6 +765,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
+    ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
+                    help="N > 1: the results' all-gather over peer memory or NCCL")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the other configs and the op microbenchmarks (N = 1)")
     args = ap.parse_args()

@@ -269,6 +269,43 @@ int vtnk_trie_fill(int64_t n_items, int64_t levels, int64_t vocab, int64_t dense
                    int64_t* row_ptrs, int64_t* cols_vals, int64_t* layer_max_branches,
                    uint8_t* const* dense_masks, int64_t* dense_states, void* stream);
 
+/* Result all-gather over peer memory for the batch-sharded search (replaces
+ * the NCCL all-gather of the ranks' results; the reference has no
+ * multi-GPU path).  Every rank owns a gather buffer of 2 * world *
+ * record_bytes bytes and a flag array of 8 uint32 words (both zeroed before
+ * the first call, opened on the other ranks through the IPC helpers below),
+ * plus two local uint32 epoch words and one int status word (zeroed).
+ * vtnk_peer_gather packs this rank's search result (ids int64 [n, levels],
+ * logp fp32 [n], node int64 [n]) into the record layout
+ *   ids int32 [n, levels] | node int32 [n] | logp fp32 [n]   (16-byte aligned regions)
+ * stores it into slot `rank` of half (e & 1) of every rank's buffer, where e
+ * counts this rank's calls from 1, then waits -- bounded by wait_ns (0: 2 s)
+ * -- until every rank has pushed its record e.  On return (stream order)
+ * half (e & 1) of this rank's buffer holds every rank's record, valid until
+ * this rank's call after next.  status: 1 = a wait ran out, 2 = an id did not
+ * fit int32.  world <= 8; plain stores over NVLink, no multicast. */
+typedef struct {
+  int32_t world;
+  int32_t rank;
+  int64_t record_bytes;    /* >= vtnk_peer_record_bytes(n, levels) */
+  void* records[8];        /* every rank's gather buffer, as mapped in this process */
+  uint32_t* flags[8];      /* every rank's flag array, as mapped in this process */
+  uint32_t* epoch;         /* this rank's 2 epoch words (device) */
+  int* status;             /* this rank's status word (device) */
+  uint64_t wait_ns;
+} vtnk_peer_group_t;
+
+int64_t vtnk_peer_record_bytes(int64_t n, int64_t levels);
+int vtnk_peer_gather(const vtnk_peer_group_t* g, const int64_t* ids, const float* logp,
+                     const int64_t* node, int64_t n, int64_t levels, void* stream);
+/* CUDA IPC helpers for setting up a peer group (one process per GPU).  The
+ * handle names the allocation that holds dev_ptr; offset_out is dev_ptr's
+ * offset inside it, to be added to the pointer the peer opens. */
+int vtnk_ipc_handle_bytes(void);
+int vtnk_ipc_get_handle(const void* dev_ptr, void* handle_out, int64_t* offset_out);
+int vtnk_ipc_open_handle(const void* handle, void** dev_ptr_out);
+int vtnk_ipc_close_handle(void* dev_ptr);
+
 /* Synthetic hidden states (benchmark / test input generator, no reference
  * counterpart): out[r, h] = table[mix64(key(seed, stream_id) ^ ((row0 + r) * H + h)) >> 48]
  * with the 65,536-entry quantile table given as bf16 bits (dtype BF16) or fp32

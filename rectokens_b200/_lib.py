@@ -39,6 +39,12 @@ EXPORTS = (
     "vtnk_trie_workspace_bytes",
     "vtnk_trie_count",
     "vtnk_trie_fill",
+    "vtnk_peer_record_bytes",
+    "vtnk_peer_gather",
+    "vtnk_ipc_handle_bytes",
+    "vtnk_ipc_get_handle",
+    "vtnk_ipc_open_handle",
+    "vtnk_ipc_close_handle",
     "vtnk_device_status",
     "vtnk_set_wait_limit_ns",
     "vtnk_debug_stall_launches",
@@ -69,6 +75,12 @@ class Search(ctypes.Structure):
                 ("dtype", c_int32), ("csr", Csr), ("layer_max_branches", POINTER(c_int64)),
                 ("index", POINTER(ChildIndex)),
                 ("levels", c_int64), ("batch", c_int64), ("beams", c_int64), ("n_cand", c_int64)]
+
+
+class PeerGroup(ctypes.Structure):
+    _fields_ = [("world", c_int32), ("rank", c_int32), ("record_bytes", c_int64),
+                ("records", c_void_p * 8), ("flags", c_void_p * 8), ("epoch", c_void_p),
+                ("status", c_void_p), ("wait_ns", c_uint64)]
 
 
 _lib = None
@@ -114,6 +126,18 @@ def lib() -> ctypes.CDLL:
             fn = getattr(L, name)
             fn.argtypes = args
             fn.restype = c_int
+        L.vtnk_peer_record_bytes.argtypes = [I64, I64]
+        L.vtnk_peer_record_bytes.restype = c_int64
+        L.vtnk_peer_gather.argtypes = [POINTER(PeerGroup), P, P, P, I64, I64, V]
+        L.vtnk_peer_gather.restype = c_int
+        L.vtnk_ipc_handle_bytes.argtypes = []
+        L.vtnk_ipc_handle_bytes.restype = c_int
+        L.vtnk_ipc_get_handle.argtypes = [P, P, POINTER(c_int64)]
+        L.vtnk_ipc_get_handle.restype = c_int
+        L.vtnk_ipc_open_handle.argtypes = [P, POINTER(c_void_p)]
+        L.vtnk_ipc_open_handle.restype = c_int
+        L.vtnk_ipc_close_handle.argtypes = [P]
+        L.vtnk_ipc_close_handle.restype = c_int
         L.vtnk_trie_workspace_bytes.argtypes = [I64, I64]
         L.vtnk_trie_workspace_bytes.restype = c_size_t
         L.vtnk_beam_search_workspace_bytes.argtypes = [POINTER(Search)]
