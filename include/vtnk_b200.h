@@ -177,6 +177,21 @@ int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk
                    int64_t* cand_tok, float* cand_logit, int64_t* cand_node, float* row_lse,
                    void* stream);
 
+/* The per-level candidate work of decode_one_step on a CSR level for a
+ * language model that returns full-vocabulary logits
+ * (rectokens/decoding/constrained_decoding.py:271-303 and 372-383: the mask
+ * op, log_softmax, topk(beam_size) and the next-node lookup), in one pass:
+ * for each row of logits [B, N] (row stride logits_stride, dtype F32 / BF16 /
+ * F16) at trie node cur_node[b] (NULL = root), the n_cand best children by
+ * logit (ties to the lower slot) with token ids and child node ids, and the
+ * row's log-sum-exp over its children -- the outputs of vtnk_beam_step, ready
+ * for vtnk_beam_merge.  Only the children's columns are read. */
+int vtnk_beam_candidates_from_logits(const void* logits, int32_t dtype, int64_t B, int64_t N,
+                                     int64_t logits_stride, const int64_t* cur_node,
+                                     const vtnk_csr_t* csr, int64_t max_branches, int64_t n_cand,
+                                     int64_t* cand_tok, float* cand_logit, int64_t* cand_node,
+                                     float* row_lse, void* stream);
+
 /* Beam merge (rectokens/decoding/constrained_decoding.py:305-349, next node
  * :368-383).  Inputs are vtnk_beam_step's outputs: a candidate whose logit is
  * -inf is missing (its token and node are -1).  level 0: each of the B

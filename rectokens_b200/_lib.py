@@ -32,6 +32,7 @@ EXPORTS = (
     "vtnk_build_child_index",
     "vtnk_beam_step",
     "vtnk_beam_merge",
+    "vtnk_beam_candidates_from_logits",
     "vtnk_beam_search_workspace_bytes",
     "vtnk_beam_search",
     "vtnk_beam_search_noalloc",
@@ -115,6 +116,8 @@ def lib() -> ctypes.CDLL:
             "vtnk_beam_step": [POINTER(Linear), P, POINTER(Csr), I64, I64, POINTER(ChildIndex),
                                P, P, P, P, V],
             "vtnk_beam_merge": [I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, V],
+            "vtnk_beam_candidates_from_logits": [P, c_int32, I64, I64, I64, P, POINTER(Csr), I64,
+                                                 I64, P, P, P, P, V],
             "vtnk_beam_search": [POINTER(Search), P, c_size_t, P, P, P, V],
             "vtnk_beam_search_noalloc": [POINTER(Search), P, P, P, V],
             "vtnk_synth_normal": [c_uint64, c_uint64, I64, I64, I64, P, c_int32, P, V],

@@ -456,6 +456,23 @@ int vtnk_beam_step(const vtnk_linear_t* lin, const int64_t* cur_node, const vtnk
                         cand_node, row_lse, true, as_stream(stream));
 }
 
+int vtnk_beam_candidates_from_logits(const void* logits, int32_t dtype, int64_t B, int64_t N,
+                                     int64_t logits_stride, const int64_t* cur_node,
+                                     const vtnk_csr_t* csr, int64_t max_branches, int64_t n_cand,
+                                     int64_t* cand_tok, float* cand_logit, int64_t* cand_node,
+                                     float* row_lse, void* stream) {
+  int rc = check_csr(csr);
+  if (rc) return rc;
+  VTNK_REQUIRE(B >= 0 && N >= 1 && logits_stride >= N, "bad logits shape");
+  VTNK_REQUIRE(max_branches >= 0 && max_branches <= (1 << 20), "max_branches out of range");
+  VTNK_REQUIRE(n_cand >= 1 && n_cand <= 1024, "n_cand out of range");
+  VTNK_REQUIRE(B == 0 || (logits && cand_tok && cand_logit && cand_node && row_lse),
+               "NULL pointer");
+  return launch_logits_beam(logits, dtype, B, N, logits_stride, cur_node, make_csr(*csr),
+                            max_branches, static_cast<int>(n_cand), cand_tok, cand_logit,
+                            cand_node, row_lse, as_stream(stream));
+}
+
 int vtnk_beam_merge(int64_t level, int64_t B, int64_t k, int64_t n_cand,
                     const int64_t* cand_tok, const float* cand_logit, const int64_t* cand_node,
                     const float* row_lse, const float* prev_logp, const int64_t* prev_ids,

@@ -122,6 +122,9 @@ int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
                 const int64_t* cur_node, const Csr& csr, int64_t mb, void* out, int64_t* nn,
                 int64_t* vi, cudaStream_t s);
 int launch_merge(const MergeArgs& p, cudaStream_t s);
+int launch_logits_beam(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
+                       const int64_t* cur_node, const Csr& csr, int64_t mb, int k,
+                       int64_t* tok, float* logit, int64_t* node, float* lse, cudaStream_t s);
 int launch_synth(uint64_t key, int64_t e0, int64_t count, const void* table, int dtype, void* out,
                  cudaStream_t s);
 int launch_gumbel(uint64_t seed, int64_t rows, int64_t mb, float* out, cudaStream_t s);

@@ -177,6 +177,66 @@ rows_kernel(const RowsArgs p) {
   }
 }
 
+// Beam candidates from precomputed logits (a language model that returns the
+// full vocabulary): per row, the children's logits are gathered from the
+// logits row (the other columns are the -inf of the reference's mask), then
+// the row's log-sum-exp over the children and its n_cand best children
+// (ties to the lower slot) with their tokens and node ids -- the work of
+// decode_one_step's mask op, log_softmax, topk(beam_size) and next-node
+// lookup in one pass (rectokens/decoding/constrained_decoding.py:271-303,
+// 372-383).  Warp per row.
+template <typename T>
+__global__ void __launch_bounds__(kWarps * 32)
+logits_beam_kernel(const T* __restrict__ logits, int64_t B, int64_t N, int64_t ls,
+                   const int64_t* __restrict__ cur_node, const Csr csr, int64_t mb, int k,
+                   int buf_cap, int64_t* __restrict__ out_tok, float* __restrict__ out_logit,
+                   int64_t* __restrict__ out_node, float* __restrict__ out_lse) {
+  extern __shared__ float smem[];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  float* buf = smem + warp * buf_cap;
+  for (int64_t row = static_cast<int64_t>(blockIdx.x) * kWarps + warp; row < B;
+       row += static_cast<int64_t>(gridDim.x) * kWarps) {
+    int64_t start;
+    int count;
+    node_children(csr, cur_node ? cur_node[row] : 0, mb, start, count);
+    for (int j = lane; j < count; j += 32) {
+      const int64_t c = __ldg(csr.cols + start + j);
+      buf[j] = (c >= 0 && c < N) ? to_f32<T>(logits[row * ls + c]) : -INFINITY;
+    }
+    __syncwarp();
+    float m = -INFINITY;
+    for (int j = lane; j < count; j += 32) m = fmaxf(m, buf[j]);
+    m = warp_max(m);
+    float sum = 0.f;
+    if (m > -INFINITY)
+      for (int j = lane; j < count; j += 32) sum += expf(buf[j] - m);
+    sum = warp_sum(sum);
+    if (lane == 0) out_lse[row] = (m > -INFINITY) ? m + logf(sum) : -INFINITY;
+    for (int r = 0; r < k; ++r) {
+      float bv = -INFINITY;
+      int bj = INT_MAX;
+      for (int j = lane; j < count; j += 32) {
+        const float v = buf[j];
+        if (v > bv || (v == bv && j < bj)) {
+          bv = v;
+          bj = j;
+        }
+      }
+      warp_argmax(bv, bj);
+      if (lane == 0) {
+        const int64_t o = row * k + r;
+        const bool ok = bj != INT_MAX && bv > -INFINITY;
+        out_logit[o] = ok ? bv : -INFINITY;
+        out_tok[o] = ok ? __ldg(csr.cols + start + bj) : -1;
+        out_node[o] = ok ? __ldg(csr.vals + start + bj) : -1;
+        if (bj != INT_MAX) buf[bj] = __int_as_float(0x7fc00000);  // taken
+      }
+      __syncwarp();
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kWarps * 32)
 mask_kernel(const T* __restrict__ logits, int64_t B, int64_t N, int64_t ls,
@@ -555,10 +615,12 @@ __global__ void __launch_bounds__(128)
 merge_group_kernel(const MergeArgs p) {
   extern __shared__ float gsm[];
   // Launched as a programmatic dependent of the step kernel (inside a
-  // search): wait for its results, then let the next level's step kernel be
-  // scheduled as this merge drains.  Both are no-ops in a plain launch.
-  asm volatile("griddepcontrol.wait;" ::: "memory");
+  // search).  The next level's step kernel may be scheduled at once: its
+  // CTAs take the SMs the step kernel's last tile round leaves idle and start
+  // streaming their operands (their epilogues wait for this merge).  Then
+  // wait for the step kernel's results.  Both are no-ops in a plain launch.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   constexpr int QPB = 128 / G;  // queries per block
   const int n = p.n_cand;
   const int L = p.level == 0 ? 1 : p.k;
@@ -684,6 +746,38 @@ int launch_mask(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
       return VTNK_ERR_ARG;
   }
   return cuda_status(cudaGetLastError(), "mask_kernel launch");
+}
+
+int launch_logits_beam(const void* logits, int dtype, int64_t B, int64_t N, int64_t ls,
+                       const int64_t* cur_node, const Csr& csr, int64_t mb, int k,
+                       int64_t* tok, float* logit, int64_t* node, float* lse, cudaStream_t s) {
+  if (B == 0) return VTNK_OK;
+  const int cap = static_cast<int>(mb > 0 ? mb : 1);
+  const size_t sm = static_cast<size_t>(kWarps) * cap * sizeof(float);
+  if (sm > 200 * 1024) {
+    set_error("max_branches too large for the candidates kernel");
+    return VTNK_ERR_UNSUPPORTED;
+  }
+  const int grid = grid_for(B, kWarps);
+#define VTNK_LB_LAUNCH(T)                                                                       \
+  do {                                                                                          \
+    if (sm > 48 * 1024)                                                                         \
+      cudaFuncSetAttribute(logits_beam_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                           static_cast<int>(sm));                                               \
+    logits_beam_kernel<T><<<grid, kWarps * 32, sm, s>>>(static_cast<const T*>(logits), B, N,   \
+                                                        ls, cur_node, csr, mb, k, cap, tok,     \
+                                                        logit, node, lse);                      \
+  } while (0)
+  switch (dtype) {
+    case VTNK_F32: VTNK_LB_LAUNCH(float); break;
+    case VTNK_BF16: VTNK_LB_LAUNCH(__nv_bfloat16); break;
+    case VTNK_F16: VTNK_LB_LAUNCH(__half); break;
+    default:
+      set_error("unsupported dtype %d", dtype);
+      return VTNK_ERR_ARG;
+  }
+#undef VTNK_LB_LAUNCH
+  return cuda_status(cudaGetLastError(), "logits_beam_kernel launch");
 }
 
 int launch_merge(const MergeArgs& p, cudaStream_t s) {

@@ -7,15 +7,15 @@ the whole vocabulary and the CSR trie masks them).  Per level:
 
 * dense levels (``step < len(trie.dense_mask_by_layer)``): the dense mask, as
   in the reference (:261-268);
-* CSR levels: the CUDA mask op ``constrained_node_transition``;
-* candidates: ``topk(beam_size)`` of the masked logits with their
-  log-softmax (:294-303; temperature > 0 samples with ``torch.multinomial``
-  exactly as the reference does);
-* beam merge and next trie node: the CUDA merge kernel (``vtnk_beam_merge``),
-  which also returns the parent row of every new beam; the child node of each
-  candidate is found on the device by matching its token against the parent's
-  ``valid_idxs`` (:372-383) -- no boolean-mask indexing, so no host
-  synchronisation per level;
+* CSR levels at temperature 0: one CUDA kernel
+  (``vtnk_beam_candidates_from_logits``) gathers each row's children's
+  logits, forms the row's log-sum-exp and its ``beam_size`` best children
+  with their node ids -- the mask op, ``log_softmax``, ``topk(beam_size)`` and
+  the next-node lookup of :271-303 and :372-383, with no host
+  synchronisation; other levels (dense, sampling) use the CUDA mask op and
+  tensor operations as the reference does (:294-303);
+* beam merge: the CUDA merge kernel (``vtnk_beam_merge``), which also returns
+  the parent row of every new beam;
 * KV cache and attention mask are reordered by the parent rows (:305-366).
 
 Route B, the ``SparseLinear`` output projection (``attr_path``; reference
@@ -75,6 +75,88 @@ def _merge(level, B, k, tok, logit, node, lse, prev_logp, prev_ids):
     return ids, logp, nxt, parent
 
 
+def _candidates(logits, cs, beam_size):
+    """``vtnk_beam_candidates_from_logits``: ``(tok, logit, node, lse)``."""
+    trie = cs.trie
+    R, N = logits.shape
+    logits = logits if logits.stride(1) == 1 else logits.contiguous()
+    dev = logits.device
+    tok = torch.empty((R, beam_size), dtype=torch.int64, device=dev)
+    logit = torch.empty((R, beam_size), dtype=torch.float32, device=dev)
+    node = torch.empty((R, beam_size), dtype=torch.int64, device=dev)
+    lse = torch.empty((R,), dtype=torch.float32, device=dev)
+    cur = cs.cur_node.contiguous()
+    csr = L.csr_struct(trie.row_ptrs, trie.stacked_cols_vals)
+    L.check(L.lib().vtnk_beam_candidates_from_logits(
+        logits.data_ptr(), L.DTYPE_CODE[logits.dtype], R, N, max(logits.stride(0), N),
+        cur.data_ptr(), csr, trie.layer_max_branches[cs.step], beam_size, tok.data_ptr(),
+        logit.data_ptr(), node.data_ptr(), lse.data_ptr(), L.stream_of(dev)))
+    return tok, logit, node, lse
+
+
+def _candidates_torch(logits, cs, config, step, n_dense, first, prev_ids, R, beam_size, sparse):
+    """Candidates of dense levels, of sampling (temperature > 0) and of the
+    routed SparseLinear strategies: ``(tok, logit, node, lse)``."""
+    trie = cs.trie
+    next_nodes = valid_idxs = None
+    if step < n_dense:
+        layer_mask = trie.dense_mask_by_layer[step]
+        if first:
+            layer_mask = layer_mask.unsqueeze(0).expand(R, -1)
+        else:
+            layer_mask = layer_mask[prev_ids.unbind(-1)]
+        masked = logits.float().masked_fill(~layer_mask, float("-inf"))
+    elif sparse is not None:
+        next_nodes, valid_idxs = sparse.next_nodes, sparse.valid_idxs
+        masked = logits.float()
+    else:
+        next_nodes, valid_idxs, masked = constrained_node_transition(logits, cs)
+        masked = masked.float()
+
+    routed = sparse is not None and (sparse.sample is not None or sparse.topk_idxs is not None)
+    if sparse is not None and sparse.sample is not None:
+        # one Gumbel-max sample per row, scored 0 (reference :281-286)
+        cand_tok = sparse.sample.long().unsqueeze(1)
+        cand_logit = torch.where(cand_tok >= 0, 0.0, float("-inf")).float()
+        lse = torch.zeros((R,), dtype=torch.float32, device=logits.device)
+    elif sparse is not None and sparse.topk_idxs is not None:
+        # the op's top beam_size children, scored by the log-softmax over
+        # those logits only (reference :287-293)
+        cand_tok = sparse.topk_idxs
+        cand_logit = masked
+        lse = torch.logsumexp(masked, dim=-1)
+    else:
+        lse = torch.logsumexp(masked, dim=-1)
+    if routed:
+        pass  # candidates come from the fused op
+    elif config.temperature == 0.0:
+        cand_logit, cand_tok = masked.topk(beam_size, dim=-1)
+    else:
+        probs = F.softmax(masked / config.temperature, dim=-1)
+        cand_tok = torch.multinomial(probs, num_samples=beam_size)
+        cand_logit = masked.gather(1, cand_tok)
+        # sampled candidates are unsorted; the merge takes its exact path for them
+    cand_tok = torch.where(cand_logit > float("-inf"), cand_tok, torch.full_like(cand_tok, -1))
+
+    if next_nodes is not None:
+        # child node of each candidate: the branch slot whose token matches
+        # (per-row sort + binary search; padding sorts last)
+        vi = torch.where(valid_idxs >= 0, valid_idxs, torch.iinfo(torch.int64).max)
+        vs, perm = torch.sort(vi, dim=1)
+        pos = torch.searchsorted(vs, cand_tok).clamp(max=vs.shape[1] - 1)
+        hit = vs.gather(1, pos) == cand_tok
+        slot = perm.gather(1, pos)
+        cand_node = torch.where(hit & (cand_tok >= 0), next_nodes.gather(1, slot), -1)
+    else:
+        cand_node = torch.full_like(cand_tok, -1)
+
+    if config.temperature != 0.0 and not routed:
+        # the reference scores sampled candidates by log(p_T) (:298-303)
+        cand_logit = torch.where(cand_tok >= 0, cand_logit / config.temperature, cand_logit)
+        lse = torch.logsumexp(masked / config.temperature, dim=-1)
+    return cand_tok, cand_logit, cand_node, lse
+
+
 @torch.inference_mode()
 def decode_one_step(
     constrained_generation_state: ConstrainedGenerationState,
@@ -112,62 +194,16 @@ def decode_one_step(
     B = R if first else R // k
     prev_ids = None if first else gen.generated_ids.reshape(B * k, -1)
 
-    next_nodes = valid_idxs = None
-    if step < n_dense:
-        layer_mask = trie.dense_mask_by_layer[step]
-        if first:
-            layer_mask = layer_mask.unsqueeze(0).expand(R, -1)
-        else:
-            layer_mask = layer_mask[prev_ids.unbind(-1)]
-        masked = logits.float().masked_fill(~layer_mask, float("-inf"))
-    elif use_sparse:
-        next_nodes, valid_idxs = sparse.next_nodes, sparse.valid_idxs
-        masked = logits.float()
-    else:
-        next_nodes, valid_idxs, masked = constrained_node_transition(logits, cs)
-        masked = masked.float()
-
     routed = use_sparse and (sparse.sample is not None or sparse.topk_idxs is not None)
-    if use_sparse and sparse.sample is not None:
-        # one Gumbel-max sample per row, scored 0 (reference :281-286)
-        cand_tok = sparse.sample.long().unsqueeze(1)
-        cand_logit = torch.where(cand_tok >= 0, 0.0, float("-inf")).float()
-        lse = torch.zeros((R,), dtype=torch.float32, device=logits.device)
-    elif use_sparse and sparse.topk_idxs is not None:
-        # the op's top beam_size children, scored by the log-softmax over
-        # those logits only (reference :287-293)
-        cand_tok = sparse.topk_idxs
-        cand_logit = masked
-        lse = torch.logsumexp(masked, dim=-1)
+    if step >= n_dense and config.temperature == 0.0 and not routed:
+        # CSR level, greedy: one kernel gathers the children's logits, forms
+        # the row log-sum-exp and the beam_size best children with their
+        # nodes (the mask op + log_softmax + topk + node lookup, :271-303)
+        cand_tok, cand_logit, cand_node, lse = _candidates(logits, cs, beam_size)
     else:
-        lse = torch.logsumexp(masked, dim=-1)
-    if routed:
-        pass  # candidates come from the fused op
-    elif config.temperature == 0.0:
-        cand_logit, cand_tok = masked.topk(beam_size, dim=-1)
-    else:
-        probs = F.softmax(masked / config.temperature, dim=-1)
-        cand_tok = torch.multinomial(probs, num_samples=beam_size)
-        cand_logit = masked.gather(1, cand_tok)
-        # sampled candidates are unsorted; the merge takes its exact path for them
-    cand_tok = torch.where(cand_logit > float("-inf"), cand_tok, torch.full_like(cand_tok, -1))
-
-    if next_nodes is not None:
-        # child node of each candidate: the branch slot whose token matches
-        # (per-row sort + binary search; padding sorts last)
-        vi = torch.where(valid_idxs >= 0, valid_idxs, torch.iinfo(torch.int64).max)
-        vs, perm = torch.sort(vi, dim=1)
-        pos = torch.searchsorted(vs, cand_tok).clamp(max=vs.shape[1] - 1)
-        hit = vs.gather(1, pos) == cand_tok
-        slot = perm.gather(1, pos)
-        cand_node = torch.where(hit & (cand_tok >= 0), next_nodes.gather(1, slot), -1)
-    else:
-        cand_node = torch.full_like(cand_tok, -1)
-
-    if config.temperature != 0.0 and not routed:
-        # the reference scores sampled candidates by log(p_T) (:298-303)
-        cand_logit = torch.where(cand_tok >= 0, cand_logit / config.temperature, cand_logit)
-        lse = torch.logsumexp(masked / config.temperature, dim=-1)
+        cand_tok, cand_logit, cand_node, lse = _candidates_torch(
+            logits, cs, config, step, n_dense, first, prev_ids, R, beam_size,
+            sparse if use_sparse else None)
 
     ids, new_logp, nxt, parent = _merge(step, B, k, cand_tok, cand_logit.float(), cand_node,
                                         lse.float(), log_probas, prev_ids)

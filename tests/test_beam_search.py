@@ -295,10 +295,16 @@ def test_sampling_search_cfg4_against_oracle(cuda_ok):
         _, vi, osmp, score = O.fused_sampling(a64, W64.T, None, rp, cv, cur[:n_chk], mb, noise,
                                               w.temperature)
         got = tk[:n_chk, level].astype(np.float32)
+        near = 0
         for r in np.nonzero(got != osmp)[0]:
             slot = np.nonzero(vi[r] == int(got[r]))[0]
             assert slot.size == 1
-            assert score[r, slot[0]] >= np.max(score[r]) - 2e-2, (level, r)
+            best = np.max(score[r])
+            # near-tie rule: within 1e-3 relative of the best Gumbel score
+            assert score[r, slot[0]] >= best - 1e-3 * max(1.0, abs(best)), (level, r)
+            near += 1
+        print(f"cfg4 level {level}: {near} near-tie samples of {n_chk}")
+        assert near <= 1
         # walk the trie along the sampled tokens
         nxt = np.empty_like(cur)
         for b in range(w.batch):

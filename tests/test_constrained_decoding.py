@@ -171,3 +171,31 @@ def test_route_b_sampling_paths_are_catalog_items(cuda_ok):
                                   cfg, attr_path="lm_head").cpu().numpy().reshape(-1, w.levels)
     items = {tuple(t) for t in S.to_tokens(codes, w.codes).tolist()}
     assert all(tuple(r) in items for r in ids.tolist())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_candidates_kernel_matches_mask_topk_path(dtype, cuda_ok):
+    """``vtnk_beam_candidates_from_logits`` (one pass over the children's
+    columns) against the mask op + log-sum-exp + topk + node lookup it
+    replaces in ``decode_one_step``, on random full-vocabulary logits at
+    every CSR depth of the cfg2 catalog (ties are absent in random data)."""
+    from rectokens_b200.decoding.constrained_decoding import _candidates, _candidates_torch
+
+    w = S.WORKLOADS["cfg2"]
+    trie = WL.build_trie(w, DEV)
+    g = torch.Generator(device=DEV).manual_seed(3)
+    cfg = GenerationConfig(steps=w.levels, k=w.beams, beam_size=w.topk, temperature=0.0)
+    from rectokens_b200.decoding.beam_search import depth_layout
+
+    for step in range(1, w.levels):
+        R = 777
+        logits = torch.randn(R, w.vocab, generator=g, device=DEV).to(dtype)
+        d = depth_layout(trie)[step]  # node ids of this depth: [node_lo, node_hi)
+        cur = torch.randint(d.node_lo, d.node_hi, (R,), generator=g, device=DEV)
+        cs = ConstraintState(step, trie, cur)
+        a = _candidates(logits, cs, w.topk)
+        b = _candidates_torch(logits, cs, cfg, step, 1, False, None, R, w.topk, None)
+        torch.testing.assert_close(a[3], b[3].float(), atol=1e-5, rtol=0)
+        assert torch.equal(a[0], b[0])
+        assert torch.equal(a[2], b[2])
+        assert torch.equal(a[1], b[1].float())

@@ -169,13 +169,21 @@ def _assert_ids_up_to_near_ties(got, want, bl, vi, rel=1e-3):
         assert abs(vg - vw) <= rel * scale, f"row {r} slot {c}: {g} ({vg}) vs {w} ({vw})"
 
 
-def _assert_samples(got, want, score, vi, tol):
-    """Sampled tokens bit-exact given the same noise, except near-ties of the
-    Gumbel scores (within ``tol``)."""
+def _assert_samples(got, want, score, vi, tol, rel=1e-3):
+    """Sampled tokens bit-exact given the same noise, except near-ties: a
+    differing sample's Gumbel score is within ``rel`` (relative) of the best,
+    or within ``tol`` (the logit tolerance scaled by 1/T).  Such rows are
+    counted, printed and capped at 1 % of the rows."""
+    near = 0
     for r in np.nonzero(got != want)[0]:
         slots = np.nonzero(vi[r] == int(got[r]))[0]
         assert slots.size == 1, f"row {r}: kernel sampled a non-child token {got[r]}"
-        assert score[r, slots[0]] >= np.max(score[r]) - tol, f"row {r}: {got[r]} vs {want[r]}"
+        best = np.max(score[r])
+        gap = best - score[r, slots[0]]
+        assert gap <= max(tol, rel * max(1.0, abs(best))), f"row {r}: {got[r]} vs {want[r]}"
+        near += 1
+    print(f"sampling: {near} near-tie rows of {got.shape[0]}")
+    assert near <= max(2, got.shape[0] // 100)
 
 
 def test_gumbel_noise_matches_oracle(cuda_ok):
