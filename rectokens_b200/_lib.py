@@ -126,35 +126,31 @@ def lib() -> ctypes.CDLL:
                                POINTER(c_void_p), P, V],
         }
         for name, args in sig.items():
-            fn = getattr(L, name)
+            fn = getattr(L, name, None)
+            if fn is None:  # an older tuning build (VTNK_LIB_PATH) lacks newer entry points
+                continue
             fn.argtypes = args
             fn.restype = c_int
-        L.vtnk_peer_record_bytes.argtypes = [I64, I64]
-        L.vtnk_peer_record_bytes.restype = c_int64
-        L.vtnk_peer_gather.argtypes = [POINTER(PeerGroup), P, P, P, I64, I64, V]
-        L.vtnk_peer_gather.restype = c_int
-        L.vtnk_ipc_handle_bytes.argtypes = []
-        L.vtnk_ipc_handle_bytes.restype = c_int
-        L.vtnk_ipc_get_handle.argtypes = [P, P, POINTER(c_int64)]
-        L.vtnk_ipc_get_handle.restype = c_int
-        L.vtnk_ipc_open_handle.argtypes = [P, POINTER(c_void_p)]
-        L.vtnk_ipc_open_handle.restype = c_int
-        L.vtnk_ipc_close_handle.argtypes = [P]
-        L.vtnk_ipc_close_handle.restype = c_int
-        L.vtnk_trie_workspace_bytes.argtypes = [I64, I64]
-        L.vtnk_trie_workspace_bytes.restype = c_size_t
-        L.vtnk_beam_search_workspace_bytes.argtypes = [POINTER(Search)]
-        L.vtnk_beam_search_workspace_bytes.restype = c_size_t
-        L.vtnk_set_wait_limit_ns.argtypes = [c_uint64]
-        L.vtnk_set_wait_limit_ns.restype = c_int
-        L.vtnk_debug_stall_launches.argtypes = [c_int]
-        L.vtnk_debug_stall_launches.restype = c_int
-        L.vtnk_device_status.argtypes = [c_int]
-        L.vtnk_device_status.restype = c_int
-        L.vtnk_last_error.argtypes = []
-        L.vtnk_last_error.restype = c_char_p
-        L.vtnk_version.argtypes = []
-        L.vtnk_version.restype = c_int
+        other = {  # name: (argtypes, restype)
+            "vtnk_peer_record_bytes": ([I64, I64], c_int64),
+            "vtnk_peer_gather": ([POINTER(PeerGroup), P, P, P, I64, I64, V], c_int),
+            "vtnk_ipc_handle_bytes": ([], c_int),
+            "vtnk_ipc_get_handle": ([P, P, POINTER(c_int64)], c_int),
+            "vtnk_ipc_open_handle": ([P, POINTER(c_void_p)], c_int),
+            "vtnk_ipc_close_handle": ([P], c_int),
+            "vtnk_trie_workspace_bytes": ([I64, I64], c_size_t),
+            "vtnk_beam_search_workspace_bytes": ([POINTER(Search)], c_size_t),
+            "vtnk_set_wait_limit_ns": ([c_uint64], c_int),
+            "vtnk_debug_stall_launches": ([c_int], c_int),
+            "vtnk_device_status": ([c_int], c_int),
+            "vtnk_last_error": ([], c_char_p),
+            "vtnk_version": ([], c_int),
+        }
+        for name, (args, res) in other.items():
+            fn = getattr(L, name, None)
+            if fn is not None:
+                fn.argtypes = args
+                fn.restype = res
         _lib = L
     return _lib
 

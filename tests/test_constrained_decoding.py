@@ -196,6 +196,11 @@ def test_candidates_kernel_matches_mask_topk_path(dtype, cuda_ok):
         a = _candidates(logits, cs, w.topk)
         b = _candidates_torch(logits, cs, cfg, step, 1, False, None, R, w.topk, None)
         torch.testing.assert_close(a[3], b[3].float(), atol=1e-5, rtol=0)
-        assert torch.equal(a[0], b[0])
-        assert torch.equal(a[2], b[2])
-        assert torch.equal(a[1], b[1].float())
+        assert torch.equal(a[1], b[1].float())          # the same logits, in order
+        # tokens equal except among equal logits (bf16 has exact ties, whose
+        # order torch.topk leaves open; the kernel takes the lower slot)
+        diff = a[0] != b[0]
+        assert bool((a[1][diff] == b[1].float()[diff]).all())
+        assert torch.equal(a[2][~diff], b[2][~diff])
+        if dtype == torch.float32:
+            assert not bool(diff.any())
