@@ -110,6 +110,13 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
   }
 }
 
+// Order-preserving 32-bit key of a float (a > b  <=>  key(a) > key(b); -0
+// and +0 share a key).  No NaN reaches the merges.
+__device__ __forceinline__ unsigned order_key(float f) {
+  const unsigned u = __float_as_uint(f + 0.0f);  // -0 -> +0
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 // ----------------------------------------------------------------- Philox noise
 // Philox4x32-10 (Salmon, Moraes, Dror & Shaw, SC'11), first output word, with
 // the lane order and constants Triton's tl.rand uses; counter (c0, 0, 0, 0),

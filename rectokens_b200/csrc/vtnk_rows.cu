@@ -476,13 +476,6 @@ merge_sorted_kernel(const MergeArgs p) {
 // round r's choice and writes output beam r.  Candidates are staged in shared
 // memory by coalesced loads of the block's queries.  A query with an
 // unsorted list is merged by its lane 0 with the exact successor scan.
-// Order-preserving 32-bit key of a float (a > b  <=>  key(a) > key(b); -0
-// and +0 share a key).  No NaN reaches the merge.
-__device__ __forceinline__ unsigned order_key(float f) {
-  const unsigned u = __float_as_uint(f + 0.0f);  // -0 -> +0
-  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-
 template <int G>
 __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm, int64_t q0,
                                                   int n, int L, int per_q) {
