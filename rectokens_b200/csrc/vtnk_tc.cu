@@ -89,26 +89,43 @@ constexpr int MAX_NC = 32;
 constexpr int THREADS = (2 + EPI_WARPS) * 32;
 constexpr uint64_t WAIT_LIMIT_NS = 2000000000ull;  // default bound of every wait: 2 s
 
-// The split variant's cross-CTA hand-off buffers (none in the pair variant).
-template <bool SPLIT>
-struct XMerge {
-  float x[4][MAX_NC + MAX_NC / 4 + 2][32];
+// A partial result (top-n, max, sum) travels between warps as rows of a
+// [*][32] table (lane = row): NC values, the NC window columns packed four to
+// a word, max, sum.
+template <int NC>
+struct ListRows {
+  static constexpr int COLS = NC;                 // first row of the packed columns
+  static constexpr int MX = NC + (NC + 3) / 4;    // the running max
+  static constexpr int SUM = MX + 1;              // the running sum
+  static constexpr int N = SUM + 1;
 };
-template <>
-struct XMerge<false> {};
 
-// SPLIT: the split-window variant (see beam_step_kernel) with one stage
-// fewer and the buffers of its cross-CTA hand-off.
-template <bool SPLIT>
-struct SharedT {
-  static constexpr int ST = SPLIT ? STAGES - 1 : STAGES;
+// The split variant's cross-CTA hand-off buffers (none in the pair variant).
+template <bool SPLIT, int NC>
+struct XMerge {
+  float x[4][ListRows<NC>::N][32];
+};
+template <int NC>
+struct XMerge<false, NC> {};
+
+// Candidate-list slots per lane of the top-n epilogue: 16, and at least NC
+// (the hand-off merge stages a warp's NC-entry list in the same slots);
+// sampling stages one whole 32-column chunk in the same buffer.
+template <bool SAMPLE, int NC>
+constexpr int cand_slots() { return SAMPLE ? 32 : (NC > 16 ? NC : 16); }
+
+// Shared memory of one CTA with ST operand stages.  SPLIT: the split-window
+// variant's cross-CTA hand-off buffers.
+template <bool SPLIT, int NC, bool SAMPLE, int ST_>
+struct SharedBody {
+  static constexpr int ST = ST_;
+  static constexpr int CS = cand_slots<SAMPLE, NC>();
   uint8_t ring[ST][STAGE_BYTES];  // 1024-aligned stages
-  float chunk_x[EPI_WARPS][32][32];    // epilogue, per warp, [slot][lane]: top-n candidate
+  float chunk_x[EPI_WARPS][CS][32];    // epilogue, per warp, [slot][lane]: top-n candidate
                                        // values (sampling: one 32-column chunk)
-  uint8_t chunk_c[EPI_WARPS][32][32];  // their window columns
-  float merge[4][MAX_NC + MAX_NC / 4 + 2][32];  // upper-half -> lower-half partial results:
-                                                // NC values, NC byte-packed columns, max, sum
-  XMerge<SPLIT> xm;  // split: window half 1 -> half 0 (empty in the pair variant)
+  uint8_t chunk_c[EPI_WARPS][CS][32];  // their window columns
+  float merge[4][ListRows<NC>::N][32];  // upper-half -> lower-half partial results
+  XMerge<SPLIT, NC> xm;  // split: window half 1 -> half 0 (empty in the pair variant)
   float bias[BN];
   uint64_t full[ST];
   uint64_t empty[ST];
@@ -124,11 +141,23 @@ struct SharedT {
   int abort;
   int sk_last;  // epilogue: this CTA finishes the current split tile
 };
-template <bool SPLIT>
-constexpr size_t smem_bytes() {
-  return sizeof(SharedT<SPLIT>) + 1024;
+constexpr size_t SMEM_LIMIT = 232448;  // 227 KB of opt-in shared memory per CTA
+// One operand stage more than STAGES when it fits beside the epilogue's
+// buffers (the operand pipeline is latency-bound: more bytes in flight help).
+template <bool SPLIT, int NC, bool SAMPLE>
+constexpr int stages_for() {
+  constexpr int base = SPLIT ? STAGES - 1 : STAGES;
+  return sizeof(SharedBody<SPLIT, NC, SAMPLE, base + 1>) + 1024 <= SMEM_LIMIT ? base + 1 : base;
 }
-static_assert(smem_bytes<false>() <= 232448 && smem_bytes<true>() <= 232448,
+template <bool SPLIT, int NC, bool SAMPLE>
+using SharedT = SharedBody<SPLIT, NC, SAMPLE, stages_for<SPLIT, NC, SAMPLE>()>;
+template <bool SPLIT, int NC, bool SAMPLE>
+constexpr size_t smem_bytes() {
+  return sizeof(SharedT<SPLIT, NC, SAMPLE>) + 1024;
+}
+static_assert(smem_bytes<false, 32, false>() <= SMEM_LIMIT &&
+                  smem_bytes<true, 32, false>() <= SMEM_LIMIT &&
+                  smem_bytes<true, 1, true>() <= SMEM_LIMIT,
               "shared memory above the 227 KB per-CTA limit");
 
 struct Params {
@@ -760,7 +789,8 @@ template <int NC, bool SAMPLE, bool SPLIT>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                  const Params p) {
-  using Shared = SharedT<SPLIT>;
+  using Shared = SharedT<SPLIT, NC, SAMPLE>;
+  using LR = ListRows<NC>;
   constexpr int ST = Shared::ST;
   constexpr int64_t TILE_ROWS = SPLIT ? BM : PAIR_M;
   constexpr int BUF_COLS = SPLIT ? BN / 2 : BN;  // TMEM columns of one accumulator
@@ -1201,7 +1231,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             const float y = ynext;
             const int col = cnext;
             ynext = j + 1 < cnt ? sv[(j + 1) * 32 + lane] : -INFINITY;
-            cnext = sc[((j + 1) & 31) * 32 + lane];
+            cnext = sc[((j + 1) % Shared::CS) * 32 + lane];
             top.insert(y, col);  // no-op for -inf / values not above the n-th best
           }
           cnt = 0;
@@ -1222,13 +1252,17 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #ifdef VTNK_TC_EXPERIMENT_NOSELECT
           pend = 0u;  // tuning experiment only: measures the pipeline without top-n work
 #endif
-          if (__any_sync(0xffffffffu, cnt + __popc(pend) > 32)) flush();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            if ((pend >> i) & 1u) {
-              sv[cnt * 32 + lane] = x[i];
-              sc[cnt * 32 + lane] = static_cast<uint8_t>(chunk * 32 + i);
-              ++cnt;
+          for (int h = 0; h < 2; ++h) {  // 16 columns at a time: at most 16 new entries
+            if (__any_sync(0xffffffffu, cnt + __popc((pend >> (16 * h)) & 0xFFFFu) > Shared::CS))
+              flush();
+#pragma unroll
+            for (int i = 16 * h; i < 16 * h + 16; ++i) {
+              if ((pend >> i) & 1u) {
+                sv[cnt * 32 + lane] = x[i];
+                sc[cnt * 32 + lane] = static_cast<uint8_t>(chunk * 32 + i);
+                ++cnt;
+              }
             }
           }
         }
@@ -1251,17 +1285,17 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           for (int q = 0; q < 4; ++q)
             if (j + q < NC) w |= static_cast<uint32_t>(top.c[j + q] & 0xFF) << (8 * q);
             else w |= 0xFFu << (8 * q);
-          store(MAX_NC + j / 4, __uint_as_float(w));
+          store(LR::COLS + j / 4, __uint_as_float(w));
         }
-        store(MAX_NC + MAX_NC / 4, mx);
-        store(MAX_NC + MAX_NC / 4 + 1, sum);
+        store(LR::MX, mx);
+        store(LR::SUM, sum);
       };
       // Merges a table written by put_list whose columns are all higher than
       // this warp's: inserting its sorted list after ours keeps ties on the
       // lower column.
       auto absorb = [&](float (*src)[32]) {
-        const float omx = src[MAX_NC + MAX_NC / 4][lane];
-        const float osum = src[MAX_NC + MAX_NC / 4 + 1][lane];
+        const float omx = src[LR::MX][lane];
+        const float osum = src[LR::SUM][lane];
         const float nm = fmaxf(mx, omx);
         sum = (mx > -INFINITY ? sum * __expf(mx - nm) : 0.f) +
               (omx > -INFINITY ? osum * __expf(omx - nm) : 0.f);
@@ -1286,7 +1320,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const int ibc = ib < NC ? ib : 0;
           const float vb = ib < NC ? src[ibc][lane] : -INFINITY;
           const int cb = static_cast<int>(
-              (__float_as_uint(src[MAX_NC + ibc / 4][lane]) >> (8 * (ibc & 3))) & 0xFFu);
+              (__float_as_uint(src[LR::COLS + ibc / 4][lane]) >> (8 * (ibc & 3))) & 0xFFu);
           const bool take_a = !(vb > va);
           const float v = take_a ? va : vb;
           top.v[j] = v;
@@ -1520,7 +1554,7 @@ template <int NC, bool SAMPLE, bool SPLIT>
 int launch_variant(const CUtensorMap& a, const CUtensorMap& w, const Params& p, int pairs,
                    bool pdl, cudaStream_t s) {
   auto k = beam_step_kernel<NC, SAMPLE, SPLIT>;
-  constexpr size_t smem = smem_bytes<SPLIT>();
+  constexpr size_t smem = smem_bytes<SPLIT, NC, SAMPLE>();
   // The shared-memory opt-in is per kernel and device; set it once each.
   static std::atomic<uint64_t> set_on{0};  // bit d: done on device d
   int dev = 0;
