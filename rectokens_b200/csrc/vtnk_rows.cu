@@ -476,11 +476,7 @@ merge_sorted_kernel(const MergeArgs p) {
 // round r's choice and writes output beam r.  Candidates are staged in shared
 // memory by coalesced loads of the block's queries.  A query with an
 // unsorted list is merged by its lane 0 with the exact successor scan.
-// STAGE: candidate logits staged in shared memory by coalesced loads (a
-// plain launch).  Inside a search (no STAGE) they are read from global memory
-// (L1-cached) so the merge needs no shared memory: its blocks then fit beside
-// the next level's step CTAs, which take almost all of an SM's shared memory.
-template <int G, bool STAGE>
+template <int G>
 __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm, int64_t q0,
                                                   int n, int L, int per_q) {
   constexpr int QPB = 128 / G;
@@ -493,7 +489,6 @@ __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm
   // flight with) the staging loads
   const float pv = (has && p.level > 0) ? p.prev_logp[row0 + li] : 0.f;
   const float ls = has ? p.row_lse[row0 + li] : 0.f;
-  if constexpr (STAGE) {
   __syncthreads();  // the previous block's readers are done with gsm
   {
     const int64_t nq64 = p.B - q0 < QPB ? p.B - q0 : QPB;
@@ -514,10 +509,9 @@ __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm
     }
   }
   __syncthreads();
-  }
   if (b >= p.B) return;                 // whole groups retire together (the last block)
   const unsigned gmask = (G == 32) ? 0xffffffffu : (0xffffu << ((threadIdx.x & 31) & 16));
-  const float* my = STAGE ? gsm + g * per_q : p.cand_logit + b * per_q;
+  const float* my = gsm + g * per_q;
   bool ok = true;
   if (has)
     for (int j = 1; j < n; ++j) ok = ok && !(my[li * n + j] > my[li * n + j - 1]);
@@ -609,16 +603,15 @@ __device__ __forceinline__ void merge_group_block(const MergeArgs& p, float* gsm
     p.out_ids[o * (p.level + 1) + t] = p.prev_ids[parent * p.level + t];
 }
 
-template <int G, bool STAGE>
+template <int G>
 __global__ void __launch_bounds__(128)
 merge_group_kernel(const MergeArgs p) {
   extern __shared__ float gsm[];
-  // Inside a search this is a programmatic dependent of the step kernel,
-  // launched with at most two blocks per SM so that every block is resident
-  // at once: each lets the next level's step kernel be scheduled right away
-  // (its CTAs take the SMs the step kernel's last tile round leaves idle and
-  // start streaming operands; their epilogues wait for this merge), then
-  // waits for the step kernel's results.  Both are no-ops in a plain launch.
+  // Launched as a programmatic dependent of the step kernel (inside a
+  // search).  The next level's step kernel may be scheduled at once: its
+  // CTAs take the SMs the step kernel's last tile round leaves idle and start
+  // streaming their operands (their epilogues wait for this merge).  Then
+  // wait for the step kernel's results.  Both are no-ops in a plain launch.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   asm volatile("griddepcontrol.wait;" ::: "memory");
   constexpr int QPB = 128 / G;  // queries per block
@@ -628,7 +621,7 @@ merge_group_kernel(const MergeArgs p) {
   // grid-stride over blocks of QPB queries
   for (int64_t q0 = static_cast<int64_t>(blockIdx.x) * QPB; q0 < p.B;
        q0 += static_cast<int64_t>(gridDim.x) * QPB) {
-    merge_group_block<G, STAGE>(p, gsm, q0, n, L, per_q);
+    merge_group_block<G>(p, gsm, q0, n, L, per_q);
   }
 }
 
@@ -666,16 +659,6 @@ __global__ void gumbel_kernel(uint64_t seed, int64_t rows, int64_t mb, float* ou
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x)
     out[i] = gumbel_at(seed, static_cast<uint32_t>(i));
-}
-
-int merge_sms() {
-  static int n = [] {
-    int dev = 0, v = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    return v;
-  }();
-  return n;
 }
 
 int grid_for(int64_t items, int per_block) {
@@ -795,14 +778,10 @@ int launch_merge(const MergeArgs& p, cudaStream_t s) {
   const int lists = p.level == 0 ? 1 : p.k;
   if (p.k <= 32 && p.level > 0) {  // one list per query at level 0: thread-per-query below
     const int G = p.k <= 16 ? 16 : 32;
-    const bool stage = !p.pdl;  // inside a search: no shared memory (see merge_group_block)
-    const size_t sm =
-        stage ? static_cast<size_t>(128 / G) * lists * p.n_cand * sizeof(float) : 0;
+    const size_t sm = static_cast<size_t>(128 / G) * lists * p.n_cand * sizeof(float);
     if (sm <= 96 * 1024) {
-      int64_t grid = (p.B + 128 / G - 1) / (128 / G);
-      if (!stage && grid > 2 * merge_sms()) grid = 2 * merge_sms();
-      auto k = G == 16 ? (stage ? merge_group_kernel<16, true> : merge_group_kernel<16, false>)
-                       : (stage ? merge_group_kernel<32, true> : merge_group_kernel<32, false>);
+      const int64_t grid = (p.B + 128 / G - 1) / (128 / G);
+      auto k = G == 16 ? merge_group_kernel<16> : merge_group_kernel<32>;
       if (sm > 48 * 1024)
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
       cudaLaunchConfig_t cfg{};
