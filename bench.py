@@ -6,9 +6,9 @@ A step = one full L-level constrained beam search over this rank's shard of
 the workload (config 5 by default: 16M-item catalog, H=3584, bf16, batch
 65,536 x 10 beams, top-k 10; `--workload cfg4` is the Gumbel-max sampled
 search), plus -- for N > 1 -- the all-gather of every rank's results (over
-peer memory by default: one push + flag-barrier kernel, on a side stream so
-that search i's gather overlaps search i + 1, two result records alternating;
-`--no-pipeline` runs it after each search, `--gather nccl` uses NCCL).
+peer memory by default: one push + flag-barrier kernel; `--gather nccl` uses
+NCCL).  Two searches are in flight on two streams, each with its own
+workspace and result record (`--no-pipeline`: one at a time).
 Inputs (trie, head rows, per-level hidden states) are resident in HBM before
 timing.  One search is captured as a CUDA graph and replayed K times after W
 warm-ups, timed with CUDA events on the launching stream.  At config 5 the
@@ -399,12 +399,13 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
         ws = torch.empty((lib.vtnk_beam_search_workspace_bytes(search),), dtype=torch.uint8,
                          device=dev)
 
-    def one_search(sp=None, r=None):
+    def one_search(sp=None, r=None, wsb=None):
         sp = sptr if sp is None else sp
         r = rec if r is None else r
+        wsb = ws if wsb is None else wsb
         if w.sampling:
             return one_sampled(sp)
-        L.check(lib.vtnk_beam_search(search, ws.data_ptr(), ws.numel(), r.ids.data_ptr(),
+        L.check(lib.vtnk_beam_search(search, wsb.data_ptr(), wsb.numel(), r.ids.data_ptr(),
                                      r.logp.data_ptr(), r.node.data_ptr(), sp))
 
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -441,15 +442,21 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
                "timed replay (its time subtracted)" if need_flush else
                "inputs larger than L2 (hidden states >= 0.47 GB per level), no flush")
     g_search = capture(lambda sp: one_search(sp=sp))
-    # N > 1 with the peer gather: consecutive searches alternate between two
-    # result records, and search i's all-gather runs on a side stream while
-    # search i + 1 computes (a search reuses a record only after that
-    # record's previous gather finished)
-    pipelined = pgather is not None and not args.no_pipeline
-    if pipelined:
+    # Two searches in flight (top-n workloads whose inputs exceed L2): search
+    # i runs on stream i % 2 with its own workspace and result record, so one
+    # search's ramp and partial last tile rounds overlap the other's kernels.
+    # At N > 1 the peer all-gathers run in search order on their own stream;
+    # a search reuses a record only after that record's previous gather.
+    inflight = 2 if (not w.sampling and not need_flush and not args.no_pipeline
+                     and (world == 1 or pgather is not None)) else 1
+    if inflight == 2:
         rec2 = ResultRecord(Bq * k, w.levels, dev)
-        g_search2 = capture(lambda sp: one_search(sp=sp, r=rec2))
-        side = torch.cuda.Stream(dev)
+        ws2 = torch.empty_like(ws)
+        g_search2 = capture(lambda sp: one_search(sp=sp, r=rec2, wsb=ws2))
+        for _ in range(2):
+            g_search2.replay()  # warm the second record and workspace
+        s2 = torch.cuda.Stream(dev)
+        gs = torch.cuda.Stream(dev) if pgather is not None else None
         ev_s = [torch.cuda.Event(), torch.cuda.Event()]
         ev_p = [torch.cuda.Event(), torch.cuda.Event()]
     g_step, g_merge = [], []
@@ -492,22 +499,29 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
             fev[s_][0].record(stream)
             flush.fill_(1)
             fev[s_][1].record(stream)
-        if pipelined:
+        if inflight == 2:
             i = s_ & 1
-            if s_ >= 2:
-                stream.wait_event(ev_p[i])  # this record's previous gather is done
-            (g_search, g_search2)[i].replay()
-            ev_s[i].record(stream)
-            side.wait_event(ev_s[i])
-            r = (rec, rec2)[i]
-            pgather.push(r.ids, r.logp, r.node, stream=side.cuda_stream)
-            ev_p[i].record(side)
+            st = (stream, s2)[i]
+            if s_ == 1:
+                s2.wait_stream(stream)  # after t_start
+            if s_ >= 2 and gs is not None:
+                st.wait_event(ev_p[i])  # this record's previous gather is done
+            with torch.cuda.stream(st):
+                (g_search, g_search2)[i].replay()
+            if gs is not None:
+                ev_s[i].record(st)
+                gs.wait_event(ev_s[i])
+                r = (rec, rec2)[i]
+                pgather.push(r.ids, r.logp, r.node, stream=gs.cuda_stream)
+                ev_p[i].record(gs)
             continue
         g_search.replay()
         if world > 1 and not w.sampling:
             do_gather()
-    if pipelined:
-        stream.wait_event(ev_p[(steps - 1) & 1])  # every gather inside the timed region
+    if inflight == 2:  # every search and gather inside the timed region
+        stream.wait_stream(s2)
+        if gs is not None:
+            stream.wait_stream(gs)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -568,7 +582,7 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     breakdown = {"search_ms": round(float(t[1].item()), 4),
                  "gather_ms": round(float(t[2].item()), 4) if gather_ms is not None else None,
                  "gather": args.gather if world > 1 else None,
-                 "gather_overlaps_next_search": bool(pipelined),
+                 "searches_in_flight": inflight,
                  "step_ms": [round(x, 4) for x in lvl_ms],
                  "merge_ms": [round(x, 4) for x in merge_ms[1:]] if not w.sampling else []}
 
@@ -794,8 +808,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--no-pipeline", action="store_true",
-                    help="N > 1, peer gather: run each search's gather after it, not overlapped "
-                         "with the next search")
+                    help="one search in flight (default: two, on two streams)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="N > 1: the results' all-gather over peer memory or NCCL")
     ap.add_argument("--no-extras", action="store_true",
@@ -830,10 +843,10 @@ def main():
     workload_cfg["l2"] = r["l2"]
     workload_cfg["timing"] = ("one search captured as a CUDA graph and replayed; per-level "
                               "times from graphs of each launch" +
-                              ("; N > 1: each search's results all-gather (peer memory, side "
-                               "stream) overlaps the next search, every gather inside the timed "
-                               "region" if r["breakdown"].get("gather_overlaps_next_search")
-                               else ""))
+                              ("; two searches in flight on two streams (own workspace and "
+                               "result record each; at N > 1 the all-gathers in order on a third "
+                               "stream), every search and gather inside the timed region"
+                               if r["breakdown"].get("searches_in_flight", 1) == 2 else ""))
 
     others = None
     if world == 1 and not args.no_extras and args.workload == "cfg5" and not args.batch:
