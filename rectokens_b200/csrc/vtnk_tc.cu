@@ -24,7 +24,8 @@
 //                                 partial result to the lower half (split variant:
 //                                 then CTA 1 to CTA 0 through distributed shared
 //                                 memory)
-// Shared memory: a 5-stage x 32 KB operand ring (4 in the split variant), the
+// Shared memory: a 5-stage x 32 KB operand ring (4 in the split variant; one
+// stage more where the epilogue's buffers leave room), the
 // epilogue's chunk staging and hand-off buffers, the window's bias, mbarriers.
 //
 // Every mbarrier wait is bounded in time; on expiry the CTA records a status
