@@ -63,27 +63,41 @@ CPU_QUERIES = {"cfg1": 4, "cfg2": 64, "cfg3": 16, "cfg4": 256, "cfg5": 64}
 TRAFFIC_PER_ROW = {"cfg5": (7437.6, 7403.3, 7491.5)}
 
 
-def _peaks():
+def _peaks(sustained: bool = False):
+    """(HBM GB/s, dense bf16 TFLOP/s, kind).  ``sustained``: the bf16 figure of
+    a seconds-long GEMM loop under the board's power cap, the denominator for
+    a kernel timed inside a long run (the step kernel draws the 1 kW cap and
+    runs at ~1.3 GHz there); else the burst figure."""
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return d["hbm_gbs"], d["bf16_tflops"], "measured"
-    return 6650.0, 1590.0, "fallback"
+        tc = d.get("bf16_tflops_sustained") if sustained else None
+        return d["hbm_gbs"], tc or d["bf16_tflops"], "measured"
+    return 6650.0, 1400.0 if sustained else 1590.0, "fallback"
 
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during timing."""
+    """nvidia-smi sampling of SM clocks, power and throttle reasons.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Every sample carries nvidia-smi's own wall-clock timestamp, so a summary
+    can be restricted to a host-marked region (``mark``): the timed region
+    and the per-level breakdown are summarised separately.  A long run of
+    this step kernel draws the board's 1 kW limit and ``sw_power_cap`` lowers
+    the SM clock (to ~1.3 GHz); the summaries say so instead of a median
+    over idle samples."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
         self.proc = None
         self.lines: list[str] = []
         self.t = None
+        self.marks: dict[str, list[float]] = {}
 
     def start(self):
         try:
@@ -100,40 +114,63 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
-    def stop(self) -> dict:
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        if not self.lines:  # very short timed region: take one reading now
+    def mark(self, region: str, begin: bool):
+        """Host wall-clock bounds of a region (after a device synchronise)."""
+        self.marks.setdefault(region, [0.0, 0.0])[0 if begin else 1] = time.time()
+
+    def _samples(self):
+        out = []
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 10:
+                continue
             try:
-                r = subprocess.run(["nvidia-smi", f"--query-gpu={self.FIELDS}",
-                                    "--format=csv,noheader,nounits", "-i", str(self.gpu)],
-                                   capture_output=True, text=True, timeout=10)
-                self.lines += r.stdout.strip().splitlines()
-            except (OSError, subprocess.TimeoutExpired):
-                pass
+                ts = time.mktime(time.strptime(f[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                ts += float("0." + f[0].split(".")[1]) if "." in f[0] else 0.0
+                sm, smax, pw = float(f[2]), float(f[3]), float(f[4])
+            except (ValueError, IndexError):
+                continue
+            rs = {n for n, v in zip(self.NAMES, f[6:10]) if v.lower() == "active"}
+            out.append((ts, sm, smax, pw, rs))
+        return out
+
+    def stop(self) -> None:
+        if self.proc is None:
+            return
+        time.sleep(0.1)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.t.join(timeout=2)
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+
+    def summary(self, region: str | None = None) -> dict:
+        """Median SM clock / power and the reasons seen inside ``region``
+        (all samples when None, or when the region caught no sample)."""
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        smp = self._samples()
+        sel = smp
+        if region in self.marks:
+            t0, t1 = self.marks[region]
+            inside = [x for x in smp if t0 - 0.05 <= x[0] <= t1 + 0.05]
+            sel = inside or sel
+        if not sel:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        reasons = set().union(*(x[4] for x in sel))
+        return {"sm_mhz": statistics.median(x[1] for x in sel),
+                "sm_min_mhz": min(x[1] for x in sel),
+                "sm_max_mhz": max(x[2] for x in sel),
+                "power_w_median": statistics.median(x[3] for x in sel),
+                "reasons": sorted(reasons), "samples": len(sel)}
+
+    def clock_at(self, t: float) -> float | None:
+        """SM clock of the sample nearest to host time ``t``."""
+        smp = self._samples()
+        if not smp:
+            return None
+        return min(smp, key=lambda x: abs(x[0] - t))[1]
 
 
 # --------------------------------------------------------------------------- algorithmic cost
@@ -492,6 +529,7 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(dev)
+    clocks.mark("timed", True)
     fev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(2)) for _ in range(steps)]
     t_start.record(stream)
     for s_ in range(steps):
@@ -524,16 +562,62 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
             stream.wait_stream(gs)
     t_end.record(stream)
     torch.cuda.synchronize(dev)
+    clocks.mark("timed", False)
     if world > 1:
         dist.barrier()
-    clk = clocks.stop() if not extras else None
     ms_total = t_start.elapsed_time(t_end)
     if need_flush:
         ms_total -= sum(f[0].elapsed_time(f[1]) for f in fev)
     # ---------------------------------------------------------------- breakdown
     n_lvl = max(3, min(steps, 30))
+    clocks.mark("breakdown", True)
     lvl_ms = [replay_timed(g.replay, n_lvl) for g in g_step]
     merge_ms = [0.0 if g is None else replay_timed(g.replay, n_lvl) for g in g_merge]
+    clocks.mark("breakdown", False)
+    # Sustained replay of the largest level's step kernel: launch times binned
+    # by the SM clock sampled at the time (the board's power cap lowers it).
+    sustain = None
+    if not extras and args.sustain > 0 and rank == 0:
+        lv = max(range(w.levels), key=lambda l: rows_l[l])
+        batches = []
+        t_end_s = time.time() + args.sustain
+        while time.time() < t_end_s:
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0.record(stream)
+            for _ in range(5):
+                g_step[lv].replay()
+            b1.record(stream)
+            torch.cuda.synchronize(dev)
+            batches.append((time.time(), b0.elapsed_time(b1) / 5))
+        time.sleep(1.0)  # idle: the clock recovers
+        for _ in range(3):
+            b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            b0.record(stream)
+            g_step[lv].replay()
+            b1.record(stream)
+            torch.cuda.synchronize(dev)
+            batches.append((time.time(), b0.elapsed_time(b1)))
+    if not extras:
+        clocks.stop()
+        if sustain is None and args.sustain > 0 and rank == 0:
+            bins: dict = {}
+            for tb, ms in batches:
+                mhz = clocks.clock_at(tb)
+                if mhz is None:
+                    continue
+                key = int(mhz // 100) * 100
+                bins.setdefault(key, []).append(ms)
+            sustain = {"level": lv, "seconds": args.sustain,
+                       "by_sm_mhz": [{"sm_mhz": f"{k}-{k + 99}", "launches": 5 * len(v),
+                                      "ms_median": round(statistics.median(v), 4)}
+                                     for k, v in sorted(bins.items())],
+                       "note": "the level's step kernel replayed back to back; each 5-launch "
+                               "batch binned by the nvidia-smi SM-clock sample nearest to it "
+                               "(the last entries after 1 s idle)"}
+    clk = None
+    if not extras:
+        clk = clocks.summary("timed")
+        clk["breakdown"] = clocks.summary("breakdown")
     search_ms = replay_timed(g_search.replay, n_lvl)
     gather_ms = None
     if world > 1 and not w.sampling:
@@ -546,7 +630,8 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     rows_per_rank = sum(rows_l)
     value = rows_per_rank * world / (ms_per_step / 1e3)
 
-    hbm_peak, tc_peak, peak_kind = _peaks()
+    hbm_peak, tc_peak, peak_kind = _peaks(sustained=True)
+    tc_burst = _peaks()[1]
     tot_bytes = sum(c[0] for c in costs)
     tot_flops = sum(c[1] for c in costs)
     t_step = sum(lvl_ms) / 1e3
@@ -565,7 +650,10 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
     roof["traffic_note"] = ("per-level DRAM bytes per row from a small-case ncu capture of "
                             "all three levels (profiles/tc_beam_step_cfg5.md), scaled by "
                             "this search's rows")
-    roof["peak_kind"] = f"{peak_kind} (MEASURED_PEAKS.json burst figures)"
+    roof["peak_kind"] = (f"{peak_kind}: HBM copy bandwidth and the sustained bf16 GEMM figure "
+                         "(the kernels are timed in back-to-back replays, where the board's "
+                         "power cap holds the SM clock near 1.3 GHz; see clocks.breakdown)")
+    roof["tensor_frac_burst"] = (tot_flops / t_step / 1e12) / tc_burst
     roof["kernel"] = "vtnk beam-step kernel, all levels of one search"
     roof["tensor_frac"] = (tot_flops / t_step / 1e12) / tc_peak
     roof["hbm_frac"] = (tot_bytes / t_step / 1e9) / hbm_peak
@@ -710,6 +798,8 @@ def run_workload(args, w, name, dev, rank, world, extras=False):
         del host
 
     launches = steps * (w.levels if w.sampling else 2 * w.levels - 1)
+    if sustain is not None:
+        roof["sustained"] = sustain
     return dict(value=value, ms_per_step=ms_per_step, steps=steps, warmup=warm, clocks=clk,
                 roofline=roof, e2e=e2e, parity=parity, breakdown=breakdown,
                 gpu_launches=launches, l2=l2_note, dtype="bf16" if w.dtype == "bf16" else "f32")
@@ -811,6 +901,9 @@ def main():
                     help="one search in flight (default: two, on two streams)")
     ap.add_argument("--gather", default="peer", choices=["peer", "nccl"],
                     help="N > 1: the results' all-gather over peer memory or NCCL")
+    ap.add_argument("--sustain", type=float, default=3.0,
+                    help="seconds of back-to-back replays of the largest level's step kernel, "
+                         "binned by SM clock (0: skip)")
     ap.add_argument("--no-extras", action="store_true",
                     help="skip the other configs and the op microbenchmarks (N = 1)")
     args = ap.parse_args()
