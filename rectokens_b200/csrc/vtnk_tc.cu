@@ -52,7 +52,7 @@ __device__ unsigned long long g_prof[8];
 #define PROF_ACC(acc, t0) acc += clock64() - (t0)
 #define PROF_FLUSH(i, acc) atomicAdd(&g_prof[i], static_cast<unsigned long long>(acc))
 // Per-CTA %globaltimer stamps of one launch's first tile (tuning builds).
-__device__ unsigned long long g_trace[512][16];
+__device__ unsigned long long g_trace[512][32];
 #define TRACE(i)                                                                  \
   do {                                                                            \
     if (blockIdx.x < 512) {                                                       \
@@ -61,8 +61,13 @@ __device__ unsigned long long g_trace[512][16];
       g_trace[blockIdx.x][i] = t_;                                                \
     }                                                                             \
   } while (0)
+#define TRACE_VAL(i, v)                                                           \
+  do {                                                                            \
+    if (blockIdx.x < 512) g_trace[blockIdx.x][i] = static_cast<unsigned long long>(v); \
+  } while (0)
 #else
 #define TRACE(i)
+#define TRACE_VAL(i, v)
 #define PROF_T0(name)
 #define PROF_ACC(acc, t0)
 #define PROF_FLUSH(i, acc)
@@ -600,32 +605,27 @@ struct TopN {
   }
   // Larger value first; an equal value never displaces an earlier entry, so
   // feeding columns in increasing order breaks ties toward the lower column.
-  // The insert position is a count of entries >= x and every slot is then
-  // updated by an independent select from the old values: short dependency
-  // chains, so one warp per scheduler keeps issuing.
   __device__ __forceinline__ void push(float x, int col) {
     if (!(x > v[NC - 1])) return;
     insert(x, col);
   }
-  // Branch-free insert: a value not above the current n-th largest gets
-  // pos == NC and leaves the list unchanged.
+  // Branch-free insert.  ge[i] = (v[i] >= x) holds exactly for the slots
+  // before x's position (the list is sorted, and never holds a NaN: push
+  // rejects one and the candidate pass never lists one), so every slot is
+  // one select between keeping its entry, taking x, or taking its
+  // predecessor -- two dependent selects after one compare, no position
+  // count.  A value not above the n-th largest leaves the list unchanged.
   __device__ __forceinline__ void insert(float x, int col) {
-    // position = number of entries >= x, summed as a balanced tree
-    int ge[NC];
+    bool ge[NC];
 #pragma unroll
-    for (int i = 0; i < NC; ++i) ge[i] = (v[i] >= x) ? 1 : 0;
-#pragma unroll
-    for (int w = 1; w < NC; w <<= 1)
-#pragma unroll
-      for (int i = 0; i + w < NC; i += 2 * w) ge[i] += ge[i + w];
-    const int pos = ge[0];
+    for (int i = 0; i < NC; ++i) ge[i] = v[i] >= x;
 #pragma unroll
     for (int i = NC - 1; i > 0; --i) {
-      v[i] = (i > pos) ? v[i - 1] : ((i == pos) ? x : v[i]);
-      c[i] = (i > pos) ? c[i - 1] : ((i == pos) ? col : c[i]);
+      v[i] = ge[i] ? v[i] : (ge[i - 1] ? x : v[i - 1]);
+      c[i] = ge[i] ? c[i] : (ge[i - 1] ? col : c[i - 1]);
     }
-    v[0] = (pos == 0) ? x : v[0];
-    c[0] = (pos == 0) ? col : c[0];
+    v[0] = ge[0] ? v[0] : x;
+    c[0] = ge[0] ? c[0] : col;
   }
 };
 
@@ -1132,8 +1132,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
       }
 
-      TopN<NC> top;
-      top.init();
+      TopN<NC> top;  // initialised where it first comes into use (fewer live registers in pass 1)
       float mx = -INFINITY, sum = 0.f;
       const float temp = (SAMPLE && p.temperature) ? __ldg(p.temperature) : 1.f;
       if constexpr (SAMPLE) {
@@ -1141,6 +1140,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // g drawn at the reference's flat offset row * mb + slot (int32 wrap).
         // Each lane visits its children in slot order and keeps the first
         // maximum; the lower half wins ties in the hand-off below.
+        top.init();
         int pre_h = 0;  // children in the chunks before this warp's first
 #pragma unroll
         for (int i = 0; i < BN / 32; ++i) pre_h += (i < c0) ? __popc(m[i]) : 0;
@@ -1179,9 +1179,10 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         // group maximum is a lower bound of the NC-th largest value (the NC
         // largest group maxima are NC distinct entries), so pass 2 only inserts
         // values at or above it.
-        // G >= NC groups: 16 (the NC-th largest maximum by a sorting network)
-        // up to NC = 16, else NC groups (their smallest maximum).
-        constexpr int G = NC <= VTNK_TC_GROUPS ? VTNK_TC_GROUPS : NC;
+        // G >= NC groups: 16 up to NC = 16, else 32 (the NC-th largest maximum
+        // by a sorting network).  With 32 groups of 4 columns a top-20 row
+        // lists ~27 candidates per lane; with 20 groups of ~6, ~54.
+        constexpr int G = NC <= VTNK_TC_GROUPS ? VTNK_TC_GROUPS : 32;
         float gm[G];
 #pragma unroll
         for (int g = 0; g < G; ++g) gm[g] = -INFINITY;
@@ -1213,6 +1214,7 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         }
         if (warp == 2 && lane == 0 && it == 0) TRACE(8);
       const float lb = nth_largest<G, NC>(gm);
+        top.init();
         // Pass 2: the values >= lb of each lane, in column order, are appended
         // to the lane's candidate list in shared memory ([slot][lane], value
         // and window column); the list is then inserted into the top-n.  The
@@ -1222,7 +1224,9 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         float* sv = &S.chunk_x[warp - 2][0][0];
         uint8_t* sc = &S.chunk_c[warp - 2][0][0];
         int cnt = 0;
+        [[maybe_unused]] long long fl_cyc = 0, fl_cnt = 0, fl_sum = 0;
         auto flush = [&]() {
+          PROF_T0(t_fl);
           const int n = static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(cnt)));
           __syncwarp();
           float ynext = cnt > 0 ? sv[lane] : -INFINITY;
@@ -1237,6 +1241,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           }
           cnt = 0;
           __syncwarp();
+          if (warp == 2 && lane == 0 && it == 0) TRACE_VAL(14, n);
+          PROF_ACC(fl_cyc, t_fl);
+#ifdef VTNK_TC_PROFILE
+          ++fl_cnt;
+          fl_sum += n;
+#endif
         };
 #pragma unroll 1
         for (int ci = 0; ci < NCW; ++ci) {
@@ -1247,6 +1257,14 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           const int chunk = c0 + ci;
           float x[32];
           load_chunk(taddr, chunk, m, has_bias, S.bias, x);
+#ifdef VTNK_TC_PROFILE
+          if (warp == 2 && lane == 0 && it == 0) {
+            float z = 0.f;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) z += x[i];
+            if (z != 1234.5f) TRACE(16 + 2 * ci);
+          }
+#endif
           uint32_t pend = 0;
 #pragma unroll
           for (int i = 0; i < 32; ++i) pend |= (x[i] >= lb && x[i] > -INFINITY) ? (1u << i) : 0u;
@@ -1266,8 +1284,15 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
               }
             }
           }
+          if (warp == 2 && lane == 0 && it == 0) TRACE(17 + 2 * ci);
         }
+        if (warp == 2 && lane == 0 && it == 0) TRACE(13);
         flush();
+        if (warp == 2 && lane == 0 && it == 0) {
+          TRACE_VAL(26, fl_cyc);
+          TRACE_VAL(27, fl_cnt);
+          TRACE_VAL(28, fl_sum);
+        }
       }
       __syncwarp();
       release_acc(buf);
@@ -1760,7 +1785,7 @@ extern "C" int vtnk_debug_stall_launches(int n) {
 // Tuning builds only: copy (and optionally clear) the phase timers.
 extern "C" int vtnk_tc_trace(unsigned long long* out) {
   cudaDeviceSynchronize();
-  cudaMemcpyFromSymbol(out, vtnk::g_trace, sizeof(unsigned long long) * 512 * 16);
+  cudaMemcpyFromSymbol(out, vtnk::g_trace, sizeof(unsigned long long) * 512 * 32);
   return 0;
 }
 
