@@ -1160,15 +1160,22 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
 #pragma unroll
             for (int i = 0; i < 32; ++i) sx[i * 32 + lane] = x[i];
             __syncwarp();
+            // Two children per iteration, in slot order: their Philox draws
+            // are independent chains, so they overlap (a lane with one child
+            // left draws a discarded value for the second).
             uint32_t pend = mw;
             while (__any_sync(0xffffffffu, pend != 0u)) {
-              if (pend) {
-                const int i = __ffs(pend) - 1;
-                pend &= pend - 1;
-                const int slot = pre_h + __popc(mw & ((1u << i) - 1u));
-                const float g = gumbel_at(p.seed, off0 + static_cast<uint32_t>(slot));
-                top.push(sx[i * 32 + lane] / temp + g, chunk * 32 + i);
-              }
+              const int i1 = pend ? __ffs(pend) - 1 : -1;
+              pend &= pend - 1;
+              const int i2 = pend ? __ffs(pend) - 1 : -1;
+              pend &= pend - 1;
+              const int j1 = i1 < 0 ? 0 : i1, j2 = i2 < 0 ? j1 : i2;
+              const int s1 = pre_h + __popc(mw & ((1u << j1) - 1u));
+              const int s2 = pre_h + __popc(mw & ((1u << j2) - 1u));
+              const float g1 = gumbel_at(p.seed, off0 + static_cast<uint32_t>(s1));
+              const float g2 = gumbel_at(p.seed, off0 + static_cast<uint32_t>(s2));
+              if (i1 >= 0) top.push(sx[j1 * 32 + lane] / temp + g1, chunk * 32 + j1);
+              if (i2 >= 0) top.push(sx[j2 * 32 + lane] / temp + g2, chunk * 32 + j2);
             }
           }
           pre_h += __popc(mw);
