@@ -1272,18 +1272,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             if (z != 1234.5f) TRACE(16 + 2 * ci);
           }
 #endif
-#ifdef VTNK_TC_APPEND_OLD
-          uint32_t pend = 0;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) pend |= (x[i] >= lb && x[i] > -INFINITY) ? (1u << i) : 0u;
-#else
           // the candidate bits, ORed in four independent chains
           uint32_t pq[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
           for (int i = 0; i < 32; ++i)
             pq[i & 3] |= (x[i] >= lb && x[i] > -INFINITY) ? (1u << i) : 0u;
           uint32_t pend = (pq[0] | pq[1]) | (pq[2] | pq[3]);
-#endif
 #ifdef VTNK_TC_EXPERIMENT_NOSELECT
           pend = 0u;  // tuning experiment only: measures the pipeline without top-n work
 #endif
@@ -1293,13 +1287,6 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
               flush();
 #pragma unroll
             for (int i = 16 * h; i < 16 * h + 16; ++i) {
-#ifdef VTNK_TC_APPEND_OLD
-              if ((pend >> i) & 1u) {
-                sv[cnt * 32 + lane] = x[i];
-                sc[cnt * 32 + lane] = static_cast<uint8_t>(chunk * 32 + i);
-                ++cnt;
-              }
-#else
               // Branch-free: every column is written to slot cnt and counted
               // only when listed; an unlisted column's write is overwritten
               // by the next listed one or lies past the list's end (slots
@@ -1310,7 +1297,6 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
                 sc[cnt * 32 + lane] = static_cast<uint8_t>(chunk * 32 + i);
               }
               cnt += static_cast<int>((pend >> i) & 1u);
-#endif
             }
           }
           if (warp == 2 && lane == 0 && it == 0) TRACE(17 + 2 * ci);
