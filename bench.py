@@ -315,7 +315,7 @@ def reference_arm(args, w, name, workload_cfg):
     line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": 1e3 * statistics.mean(times),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "f32 (bf16 inputs upcast, as the reference's CPU path)",
             "data": "synthetic (seeded catalog / head / hidden states)", "config": workload_cfg,
             "cpu_baseline": {"value": rate, "unit": UNIT, "cores": threads, "kind": "port",
