@@ -194,6 +194,7 @@ struct Params {
   float* l0_logp;
   int64_t* l0_node;
   int l0_k;
+  int vec_out;  // outputs aligned for paired stores, n_cand and l0_k even (set by the host)
   // Schedule: tiles [0, dp_tiles) go to pairs round-robin (whole tiles); the
   // k-block iterations of tiles [dp_tiles, n_tiles) are split evenly over the
   // first sk_pairs pairs (stream-K).  A tile split between pairs is summed
@@ -1429,12 +1430,12 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           acc += __popc(m[i]);
         }
         const int64_t o = row * p.n_cand;
-#pragma unroll
-        for (int j = 0; j < NC; ++j) {
-          if (j >= p.n_cand) break;
+        // candidate j of this row: token, node id and value (-1 / -inf when none)
+        auto cand_at = [&](int j, int64_t& tok, int64_t& node, float& lv) {
           const int c = top.c[j];
-          int64_t tok = -1, node = -1;
-          float lv = -INFINITY;
+          tok = -1;
+          node = -1;
+          lv = -INFINITY;
           if (c >= 0) {
             int slot;
             if (by_slot) {
@@ -1457,19 +1458,56 @@ beam_step_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             node = (edge_ids && !by_slot) ? start + slot + 1 : __ldg(p.csr.vals + start + slot);
             lv = top.v[j];
           }
-#ifdef VTNK_TC_EXPERIMENT_NOOUT
-          if (lv != 12345.f) continue;  // tuning experiment only: outputs (almost) never stored
-#endif
-          if (p.cand_tok) p.cand_tok[o + j] = tok;
-          if (p.cand_logit) p.cand_logit[o + j] = lv;  // sampling: the winning score
-          if (p.cand_node) p.cand_node[o + j] = node;
-          if (p.l0_ids && j < p.l0_k) {  // level 0: the row's j-th best child is its beam j
-            const int64_t ob = row * p.l0_k + j;
-            p.l0_ids[ob] = tok;
-            p.l0_logp[ob] = lv > -INFINITY ? lv - lse : -INFINITY;
-            p.l0_node[ob] = node;
+        };
+        bool stored = false;
+        if constexpr (NC % 2 == 0) {
+          // Two candidates per store (16-byte token / node pairs, 8-byte value
+          // pairs) when the host found every output aligned and n_cand (and
+          // the level-0 beam count) even: half the store instructions and
+          // the L2 sectors of the lane-per-row layout.
+          if (p.vec_out) {
+#pragma unroll
+            for (int j = 0; j < NC; j += 2) {
+              if (j >= p.n_cand) break;
+              int64_t t0, t1, n0, n1;
+              float v0, v1;
+              cand_at(j, t0, n0, v0);
+              cand_at(j + 1, t1, n1, v1);
+              if (p.cand_tok) *reinterpret_cast<longlong2*>(p.cand_tok + o + j) = make_longlong2(t0, t1);
+              if (p.cand_logit) *reinterpret_cast<float2*>(p.cand_logit + o + j) = make_float2(v0, v1);
+              if (p.cand_node) *reinterpret_cast<longlong2*>(p.cand_node + o + j) = make_longlong2(n0, n1);
+              if (p.l0_ids && j < p.l0_k) {  // level 0: the row's j-th best child is its beam j
+                const int64_t ob = row * p.l0_k + j;
+                *reinterpret_cast<longlong2*>(p.l0_ids + ob) = make_longlong2(t0, t1);
+                *reinterpret_cast<float2*>(p.l0_logp + ob) =
+                    make_float2(v0 > -INFINITY ? v0 - lse : -INFINITY, v1 > -INFINITY ? v1 - lse : -INFINITY);
+                *reinterpret_cast<longlong2*>(p.l0_node + ob) = make_longlong2(n0, n1);
+              }
+            }
+            stored = true;
           }
-          if (SAMPLE && p.sample_f) p.sample_f[row] = tok >= 0 ? static_cast<float>(tok) : -1.f;
+        }
+        if (!stored) {
+#pragma unroll
+          for (int j = 0; j < NC; ++j) {
+            if (j >= p.n_cand) break;
+            int64_t tok, node;
+            float lv;
+            cand_at(j, tok, node, lv);
+#ifdef VTNK_TC_EXPERIMENT_NOOUT
+            if (lv != 12345.f) continue;  // tuning experiment only: outputs (almost) never stored
+#endif
+            if (p.cand_tok) p.cand_tok[o + j] = tok;
+            if (p.cand_logit) p.cand_logit[o + j] = lv;  // sampling: the winning score
+            if (p.cand_node) p.cand_node[o + j] = node;
+            if (p.l0_ids && j < p.l0_k) {  // level 0: the row's j-th best child is its beam j
+              const int64_t ob = row * p.l0_k + j;
+              p.l0_ids[ob] = tok;
+              p.l0_logp[ob] = lv > -INFINITY ? lv - lse : -INFINITY;
+              p.l0_node[ob] = node;
+            }
+            if (SAMPLE && p.sample_f) p.sample_f[row] = tok >= 0 ? static_cast<float>(tok) : -1.f;
+          }
         }
         if (p.row_lse) p.row_lse[row] = lse;
       }
@@ -1681,6 +1719,18 @@ int launch_beam_step_tc(const TcArgs& t, cudaStream_t s) {
   p.l0_logp = t.l0_logp;
   p.l0_node = t.l0_node;
   p.l0_k = t.l0_k;
+  {
+    auto aligned = [](const void* q, uintptr_t a) {
+      return q == nullptr || reinterpret_cast<uintptr_t>(q) % a == 0;
+    };
+    const bool l0_ok = t.l0_ids == nullptr ||
+                       (t.l0_k % 2 == 0 && aligned(t.l0_ids, 16) && aligned(t.l0_node, 16) &&
+                        aligned(t.l0_logp, 8));
+    p.vec_out = (t.n_cand % 2 == 0 && aligned(t.cand_tok, 16) && aligned(t.cand_node, 16) &&
+                 aligned(t.cand_logit, 8) && l0_ok)
+                    ? 1
+                    : 0;
+  }
   p.wait_ns = g_wait_limit_ns.load(std::memory_order_relaxed);
   for (int n = g_stall_launches.load(); n > 0;)
     if (g_stall_launches.compare_exchange_weak(n, n - 1)) {
