@@ -60,7 +60,7 @@ CPU_QUERIES = {"cfg1": 4, "cfg2": 64, "cfg3": 16, "cfg4": 256, "cfg5": 64}
 # level, from the committed small-case ncu capture of all three levels
 # (profiles/tc_beam_step_cfg5.md: batch 8192, dram__bytes_read/write.sum);
 # scaled by the rows of a full-size launch.
-TRAFFIC_PER_ROW = {"cfg5": (7431.2, 7421.6, 7519.9)}
+TRAFFIC_PER_ROW = {"cfg5": (7430.0, 7424.7, 7527.4)}
 
 
 def _peaks(sustained: bool = False):
